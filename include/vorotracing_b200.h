@@ -1,0 +1,161 @@
+/*
+ * vorotracing_b200.h -- C ABI of the B200-native Voronoi ray-traversal library
+ * (libvorotracing_b200.so).
+ *
+ * Plain pointers and sizes only.  Every pointer named *device* is CUDA global
+ * memory on the current device; every call is asynchronous on `stream`
+ * (0 = legacy default stream) and allocates nothing: outputs and scratch are
+ * passed in by the caller, scratch sizes come from the *_bytes queries.
+ * Calls return VT_OK or an error code; vt_last_error() returns the message
+ * of the last failure on the calling thread.  Errors found by kernels in the
+ * data (bad CSR, degree overflow, start index out of range) are written to
+ * the optional device word `err` as a vt_status and become visible after the
+ * stream is synchronised.
+ *
+ * Reference interfaces replaced (paths inside the VoroTracing project):
+ *   vt_prefetch_adj        trace_vorotracing_prefetch_adj, vorotracing/cuda/csrc/tracing/tracing_octmap.h:33-36
+ *   vt_trace_infer_f16     trace_vorotracing_infer,        tracing_octmap.h:38-51
+ *   vt_trace_infer_q8      trace_vorotracing_infer_q8,     tracing_octmap.h:53-67
+ *   vt_trace_fwd           trace_vorotracing_fwd,          tracing_octmap.h:11-31
+ *   vt_trace_bwd           trace_vorotracing_bwd,          tracing_octmap.h:69-91
+ *   vt_bvh_build/query     NNBVH::build / NNBVH::query,    vorotracing/cuda/csrc/utils/nn_bvh.h:4-18
+ *   vt_morton_*, vt_permute_csr      VoroTracingInfer._reorder_by_morton, vorotracing/vorotracing.py:514-571
+ *   vt_tile_perm           VoroTracingInfer._tile_perm,    vorotracing.py:606-625
+ *   vt_pad_f16x4           VoroTracingInfer._pad_3to4,     vorotracing.py:505-512
+ *   vt_minmax_f32, vt_quantize_u8    VoroTracingInfer._quantize_to_uint8, vorotracing.py:495-503
+ */
+#ifndef VOROTRACING_B200_H
+#define VOROTRACING_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define VT_API __attribute__((visibility("default")))
+#else
+#define VT_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef int vt_status;
+#define VT_OK 0
+#define VT_ERR_INVALID 1 /* bad argument (null pointer, size, alignment) */
+#define VT_ERR_CUDA 2    /* CUDA runtime error */
+#define VT_ERR_DATA 3    /* inconsistent scene data found by a kernel */
+
+typedef struct CUstream_st *vt_stream; /* == cudaStream_t */
+
+/* Message of the last failed call on this thread ("" if none). */
+VT_API const char *vt_last_error(void);
+/* Library version, e.g. "0.1.0". */
+VT_API const char *vt_version(void);
+
+/* Scene in device memory.  points (N,3) f32, density (N) f32, offsets (N+1)
+ * u32 CSR, faces = packed face rows written by vt_prefetch_adj. */
+typedef struct {
+    const float *points;
+    const float *density;
+    const uint32_t *offsets;
+    const void *faces;
+    uint32_t num_points;
+    uint64_t num_face_rows;
+} vt_scene;
+
+/* Optional per-ray diagnostics (any field may be null). */
+typedef struct {
+    uint32_t *seq;               /* (rays, seq_cap) visited cell ids */
+    uint32_t seq_cap;
+    uint32_t *seq_len;           /* (rays) cells visited */
+    uint32_t *stats;             /* (rays, 4) steps, faces tested, segments, textured */
+    uint32_t *num_intersections; /* (rays) walk step count as the reference returns it */
+} vt_debug;
+
+/* ---- packed faces (replaces the reference's adj_diff half4 rows) ---- */
+
+/* Rows of 16 bytes needed for a CSR with `csr_entries` = offsets[N] entries. */
+VT_API uint64_t vt_face_rows(uint64_t csr_entries);
+/* Build the packed face rows: per CSR entry e of cell i, half(points[adj[e]] -
+ * points[i]), the neighbour id, its CSR begin and its degree.  csr_entries =
+ * offsets[N] (read on the host by the caller). */
+VT_API vt_status vt_prefetch_adj(const float *points, uint32_t num_points, const uint32_t *adjacency,
+                          uint64_t adjacency_len, const uint32_t *offsets, uint64_t csr_entries,
+                          void *faces, uint64_t face_rows, uint32_t *err, vt_stream stream);
+
+/* ---- inference ---- */
+
+/* fp16 inference.  diffuse/specular: (N, 4*res*res) binary16 (Half4Texel:
+ * rgb + zero pad).  rays (num_rays, 6) f32, 8-byte aligned.  start (num_rays)
+ * u32.  ray_perm (num_rays) u32 or null (thread t traces ray ray_perm[t]).
+ * rgba (num_rays, 4) binary16 out, in ray order.  res = 4 or 8. */
+VT_API vt_status vt_trace_infer_f16(const vt_scene *scene, const void *diffuse, const void *specular,
+                             int res, const float *rays, uint32_t num_rays, const uint32_t *start,
+                             const uint32_t *ray_perm, float weight_threshold,
+                             uint32_t max_intersections, float cell_skip_threshold, void *rgba,
+                             const vt_debug *debug, uint32_t *err, vt_stream stream);
+
+/* q8 inference.  diffuse/specular (N, 3*res*res) u8 with one global scale and
+ * offset per map: value = scale * q + offset. */
+VT_API vt_status vt_trace_infer_q8(const vt_scene *scene, const uint8_t *diffuse, const uint8_t *specular,
+                            int res, float diff_scale, float diff_offset, float spec_scale,
+                            float spec_offset, const float *rays, uint32_t num_rays,
+                            const uint32_t *start, const uint32_t *ray_perm,
+                            float weight_threshold, uint32_t max_intersections,
+                            float cell_skip_threshold, void *rgba, const vt_debug *debug,
+                            uint32_t *err, vt_stream stream);
+
+/* ---- ray-origin cell lookup (nearest site) ---- */
+
+/* Size of the BVH blob (internal nodes + leaf ids) for num_points sites. */
+VT_API uint64_t vt_bvh_nodes_bytes(uint32_t num_points);
+/* Scratch needed by vt_bvh_build. */
+VT_API uint64_t vt_bvh_workspace_bytes(uint32_t num_points);
+/* Build the BVH over points (N,3) f32 into `nodes` (256-byte aligned). */
+VT_API vt_status vt_bvh_build(const float *points, uint32_t num_points, void *nodes,
+                              uint64_t nodes_bytes, void *workspace, uint64_t workspace_bytes,
+                              vt_stream stream);
+/* out[q] = index of the site nearest to queries[q] (squared distance in
+ * binary32, ties to the lowest index), int32. */
+VT_API vt_status vt_bvh_query(const void *nodes, const float *points, uint32_t num_points,
+                              const float *queries, uint32_t num_queries, int32_t *out,
+                              uint32_t *err, vt_stream stream);
+
+/* ---- layout transforms ---- */
+
+/* Column-wise min and max of a (rows, cols<=4) f32 matrix -> out[2*c], out[2*c+1].
+ * workspace: 256 bytes. */
+VT_API vt_status vt_minmax_f32(const float *x, uint64_t rows, int cols, void *workspace,
+                               float *out, vt_stream stream);
+/* Scratch for vt_morton_codes / vt_morton_perm / vt_permute_csr. */
+VT_API uint64_t vt_morton_workspace_bytes(uint32_t num_points);
+/* 30-bit Morton codes (int64) of the bbox-normalised sites. */
+VT_API vt_status vt_morton_codes(const float *points, uint32_t num_points, int64_t *codes,
+                                 void *workspace, vt_stream stream);
+/* perm = stable argsort(codes), inv_perm[perm[i]] = i (u32). */
+VT_API vt_status vt_morton_perm(const int64_t *codes, uint32_t num_points, uint32_t *perm,
+                                uint32_t *inv_perm, void *workspace, uint64_t workspace_bytes,
+                                vt_stream stream);
+/* dst row i = src row perm[i], rows of row_bytes bytes. */
+VT_API vt_status vt_gather_rows(const void *src, void *dst, const uint32_t *perm, uint32_t num_rows,
+                                uint32_t row_bytes, vt_stream stream);
+/* CSR of the permuted scene: new row i = old row perm[i], ids mapped by inv_perm. */
+VT_API vt_status vt_permute_csr(const uint32_t *offsets, const uint32_t *adjacency,
+                                uint32_t num_points, const uint32_t *perm, const uint32_t *inv_perm,
+                                uint32_t *new_offsets, uint32_t *new_adjacency, void *workspace,
+                                uint64_t workspace_bytes, vt_stream stream);
+/* Thread-to-pixel order of tile_h x tile_w warp tiles over a height x width image. */
+VT_API vt_status vt_tile_perm(uint32_t height, uint32_t width, uint32_t tile_h, uint32_t tile_w,
+                              uint32_t *perm, vt_stream stream);
+/* f32 rgb texels -> binary16 Half4Texel rows (rgb + zero pad). */
+VT_API vt_status vt_pad_f16x4(const float *src, uint64_t texels, void *dst, vt_stream stream);
+/* dst = clamp(rint((src - offset) / scale), 0, 255). */
+VT_API vt_status vt_quantize_u8(const float *src, uint64_t count, float scale, float offset,
+                                uint8_t *dst, vt_stream stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

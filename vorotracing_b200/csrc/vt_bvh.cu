@@ -1,0 +1,352 @@
+// vt_bvh.cu -- nearest-site BVH for the ray-origin cell lookup.
+//
+// Replaces the reference's cuBQL binary BVH and findClosest query
+// (vorotracing/cuda/csrc/utils/nn_bvh.cu:12-117).  Build: 30-bit Morton
+// codes of the sites, a stable radix sort of (code, id), Karras' (HPG 2012)
+// parallel construction of the binary radix tree (codes are disambiguated by
+// their sorted position), and a bottom-up box pass in which the second child
+// to arrive at a node computes its box (an atomic counter, no waiting).
+// Query: depth-first, nearest child first, pruning subtrees whose box is
+// strictly farther than the best site so far.
+//
+// Exact contract (matches the CPU oracle's brute force): the answer minimises
+// d2 = (dx*dx + dy*dy) + dz*dz in binary32, ties to the lowest site index.
+// The box bound is computed with the same rounded operations, and RN is
+// monotone, so a box bound never exceeds the d2 of any site inside it.
+//
+// Blob layout written by vt_bvh_build (vt_bvh_nodes_bytes(n) bytes):
+//   Node nodes[n-1]   internal nodes (32 B: box + two child links)
+//   uint32 ids[n]     site id of each leaf (sorted order)
+// A child link with bit 31 set names leaf (link & 0x7fffffff).
+#include <cub/device/device_radix_sort.cuh>
+
+#include "vt_abi.cuh"
+#include "vt_geom.cuh"
+
+namespace vt {
+namespace bvh {
+
+struct __align__(16) Node {
+    float lo[3];
+    uint32_t left;
+    float hi[3];
+    uint32_t right;
+};
+
+constexpr uint32_t kLeaf = 0x80000000u;
+constexpr int kStack = 96;
+
+__device__ __forceinline__ int f2ord(float f)
+{
+    int i = __float_as_int(f);
+    return i >= 0 ? i : i ^ 0x7fffffff;
+}
+__device__ __forceinline__ float ord2f(int i) { return __int_as_float(i >= 0 ? i : i ^ 0x7fffffff); }
+
+__global__ void bbox_init(int *bb)
+{
+    if (threadIdx.x < 3) bb[threadIdx.x] = 0x7fffffff;
+    else if (threadIdx.x < 6) bb[threadIdx.x] = (int)0x80000000;
+}
+
+__global__ void bbox_kernel(const float *__restrict__ p, uint32_t n, int *bb)
+{
+    float lo[3] = {3.4e38f, 3.4e38f, 3.4e38f}, hi[3] = {-3.4e38f, -3.4e38f, -3.4e38f};
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+        for (int a = 0; a < 3; ++a) {
+            float v = __ldg(p + (size_t)i * 3 + a);
+            lo[a] = fminf(lo[a], v);
+            hi[a] = fmaxf(hi[a], v);
+        }
+    for (int a = 0; a < 3; ++a)
+        for (int o = 16; o; o >>= 1) {
+            lo[a] = fminf(lo[a], __shfl_xor_sync(0xffffffffu, lo[a], o));
+            hi[a] = fmaxf(hi[a], __shfl_xor_sync(0xffffffffu, hi[a], o));
+        }
+    if ((threadIdx.x & 31) == 0)
+        for (int a = 0; a < 3; ++a) {
+            atomicMin(bb + a, f2ord(lo[a]));
+            atomicMax(bb + 3 + a, f2ord(hi[a]));
+        }
+}
+
+__device__ __forceinline__ uint32_t spread10(uint32_t v)
+{
+    v &= 0x3ffu;
+    v = (v | (v << 16)) & 0x030000ffu;
+    v = (v | (v << 8)) & 0x0300f00fu;
+    v = (v | (v << 4)) & 0x030c30c3u;
+    v = (v | (v << 2)) & 0x09249249u;
+    return v;
+}
+
+__global__ void morton_kernel(const float *__restrict__ p, uint32_t n, const int *bb,
+                              uint32_t *codes, uint32_t *ids)
+{
+    uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    uint32_t c = 0;
+    for (int a = 0; a < 3; ++a) {
+        float lo = ord2f(bb[a]), hi = ord2f(bb[3 + a]);
+        float ext = fmaxf(hi - lo, 1e-20f);
+        float x = (__ldg(p + (size_t)i * 3 + a) - lo) / ext * 1023.0f;
+        uint32_t q = (uint32_t)fminf(fmaxf(x, 0.0f), 1023.0f);
+        c |= spread10(q) << a;
+    }
+    codes[i] = c;
+    ids[i] = i;
+}
+
+__device__ __forceinline__ int delta(const uint32_t *codes, int n, int i, int j)
+{
+    if (j < 0 || j >= n) return -1;
+    uint32_t a = codes[i], b = codes[j];
+    if (a == b) return 32 + __clz((uint32_t)i ^ (uint32_t)j);
+    return __clz(a ^ b);
+}
+
+__global__ void karras_kernel(const uint32_t *__restrict__ codes, int n, Node *nodes,
+                              uint32_t *parent_int, uint32_t *parent_leaf, uint32_t *flags)
+{
+    int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n - 1) return;
+    int d = (delta(codes, n, i, i + 1) - delta(codes, n, i, i - 1)) >= 0 ? 1 : -1;
+    int dmin = delta(codes, n, i, i - d);
+    int lmax = 2;
+    while (delta(codes, n, i, i + lmax * d) > dmin) lmax <<= 1;
+    int l = 0;
+    for (int t = lmax >> 1; t >= 1; t >>= 1)
+        if (delta(codes, n, i, i + (l + t) * d) > dmin) l += t;
+    int j = i + l * d;
+    int dnode = delta(codes, n, i, j);
+    int s = 0;
+    for (int div = 2;; div <<= 1) {
+        int t = (l + div - 1) / div;
+        if (delta(codes, n, i, i + (s + t) * d) > dnode) s += t;
+        if (t == 1) break;
+    }
+    int g = i + s * d + (d < 0 ? -1 : 0);
+    int lo = min(i, j), hi = max(i, j);
+    uint32_t left = (lo == g) ? (kLeaf | (uint32_t)g) : (uint32_t)g;
+    uint32_t right = (hi == g + 1) ? (kLeaf | (uint32_t)(g + 1)) : (uint32_t)(g + 1);
+    nodes[i].left = left;
+    nodes[i].right = right;
+    if (left & kLeaf) parent_leaf[g] = i; else parent_int[g] = i;
+    if (right & kLeaf) parent_leaf[g + 1] = i; else parent_int[g + 1] = i;
+    flags[i] = 0;
+}
+
+__device__ __forceinline__ void child_box(const Node *nodes, const uint32_t *ids,
+                                          const float *p, uint32_t link, float lo[3], float hi[3])
+{
+    if (link & kLeaf) {
+        const float *q = p + (size_t)ids[link & ~kLeaf] * 3;
+        for (int a = 0; a < 3; ++a) lo[a] = hi[a] = q[a];
+    } else {
+        volatile const Node *c = nodes + link;
+        for (int a = 0; a < 3; ++a) {
+            lo[a] = c->lo[a];
+            hi[a] = c->hi[a];
+        }
+    }
+}
+
+__global__ void boxes_kernel(const float *__restrict__ p, int n, Node *nodes,
+                             const uint32_t *__restrict__ ids, const uint32_t *parent_int,
+                             const uint32_t *parent_leaf, uint32_t *flags)
+{
+    int k = blockIdx.x * blockDim.x + threadIdx.x;
+    if (k >= n) return;
+    uint32_t node = parent_leaf[k];
+    for (int guard = 0; guard < 2 * n; ++guard) {
+        __threadfence();
+        if (atomicAdd(flags + node, 1u) == 0) return;  // first child: the sibling finishes
+        float la[3], ha[3], lb[3], hb[3];
+        child_box(nodes, ids, p, nodes[node].left, la, ha);
+        child_box(nodes, ids, p, nodes[node].right, lb, hb);
+        for (int a = 0; a < 3; ++a) {
+            nodes[node].lo[a] = fminf(la[a], lb[a]);
+            nodes[node].hi[a] = fmaxf(ha[a], hb[a]);
+        }
+        if (node == 0) return;
+        node = parent_int[node];
+    }
+}
+
+__device__ __forceinline__ float box_d2(const Node &b, V3 q)
+{
+    float dx = fmaxf(fmaxf(b.lo[0] - q.x, 0.0f), q.x - b.hi[0]);
+    float dy = fmaxf(fmaxf(b.lo[1] - q.y, 0.0f), q.y - b.hi[1]);
+    float dz = fmaxf(fmaxf(b.lo[2] - q.z, 0.0f), q.z - b.hi[2]);
+    return (dx * dx + dy * dy) + dz * dz;
+}
+
+__device__ __forceinline__ void visit_leaf(const float *__restrict__ p, uint32_t id, V3 q,
+                                           float &best, uint32_t &bi)
+{
+    V3 d = q - ld3(p + (size_t)id * 3);
+    float d2 = dot(d, d);
+    if (d2 < best || (d2 == best && id < bi)) {
+        best = d2;
+        bi = id;
+    }
+}
+
+__global__ void query_kernel(const Node *__restrict__ nodes, const uint32_t *__restrict__ ids,
+                             const float *__restrict__ p, uint32_t n,
+                             const float *__restrict__ queries, uint32_t nq, int32_t *out,
+                             uint32_t *err)
+{
+    uint32_t t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= nq) return;
+    V3 q = mk(__ldg(queries + (size_t)t * 3), __ldg(queries + (size_t)t * 3 + 1),
+              __ldg(queries + (size_t)t * 3 + 2));
+    float best = __int_as_float(0x7f800000);
+    uint32_t bi = 0xffffffffu;
+    if (n == 1) {
+        visit_leaf(p, 0, q, best, bi);
+        out[t] = (int32_t)bi;
+        return;
+    }
+    uint32_t stack[kStack];
+    int sp = 0;
+    uint32_t cur = 0;
+    for (;;) {
+        if (cur & kLeaf) {
+            visit_leaf(p, __ldg(ids + (cur & ~kLeaf)), q, best, bi);
+        } else {
+            const Node nd = nodes[cur];
+            uint32_t c[2] = {nd.left, nd.right};
+            float dd[2];
+            for (int k = 0; k < 2; ++k) {
+                if (c[k] & kLeaf) {
+                    V3 dv = q - ld3(p + (size_t)__ldg(ids + (c[k] & ~kLeaf)) * 3);
+                    dd[k] = dot(dv, dv);
+                } else {
+                    dd[k] = box_d2(nodes[c[k]], q);
+                }
+            }
+            int nearf = dd[1] < dd[0] ? 1 : 0;
+            bool go_near = dd[nearf] <= best;
+            bool go_far = dd[1 - nearf] <= best;
+            if (go_far) {
+                if (sp >= kStack) {
+                    report(err, VT_ERR_DATA);
+                    break;
+                }
+                stack[sp++] = c[1 - nearf];
+            }
+            if (go_near) {
+                cur = c[nearf];
+                continue;
+            }
+        }
+        // pop the next subtree that can still hold a closer (or equal, lower id) site
+        bool found = false;
+        while (sp > 0) {
+            uint32_t s = stack[--sp];
+            float dd;
+            if (s & kLeaf) {
+                V3 dv = q - ld3(p + (size_t)__ldg(ids + (s & ~kLeaf)) * 3);
+                dd = dot(dv, dv);
+            } else {
+                dd = box_d2(nodes[s], q);
+            }
+            if (dd <= best) {
+                cur = s;
+                found = true;
+                break;
+            }
+        }
+        if (!found) break;
+    }
+    out[t] = (int32_t)bi;
+}
+
+inline size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+size_t sort_temp_bytes(uint32_t n)
+{
+    size_t bytes = 0;
+    cub::DeviceRadixSort::SortPairs(nullptr, bytes, (const uint32_t *)nullptr, (uint32_t *)nullptr,
+                                    (const uint32_t *)nullptr, (uint32_t *)nullptr, (int)n, 0, 30);
+    return bytes;
+}
+
+}  // namespace bvh
+}  // namespace vt
+
+using vt::bvh::align256;
+using vt::bvh::Node;
+
+extern "C" uint64_t vt_bvh_nodes_bytes(uint32_t num_points)
+{
+    return align256((size_t)(num_points ? num_points - 1 : 0) * sizeof(Node)) +
+           (size_t)num_points * 4;
+}
+
+extern "C" uint64_t vt_bvh_workspace_bytes(uint32_t n)
+{
+    return 256 + 4 * align256((size_t)n * 4) + 3 * align256((size_t)n * 4) +
+           align256(vt::bvh::sort_temp_bytes(n));
+}
+
+extern "C" vt_status vt_bvh_build(const float *points, uint32_t num_points, void *nodes,
+                                  uint64_t nodes_bytes, void *workspace, uint64_t workspace_bytes,
+                                  vt_stream stream)
+{
+    VT_REQUIRE(points && nodes && workspace, "vt_bvh_build: null pointer");
+    VT_REQUIRE(num_points > 0 && num_points < 0x7fffffffu, "vt_bvh_build: bad point count");
+    VT_REQUIRE(nodes_bytes >= vt_bvh_nodes_bytes(num_points), "vt_bvh_build: nodes buffer too small");
+    VT_REQUIRE(workspace_bytes >= vt_bvh_workspace_bytes(num_points),
+               "vt_bvh_build: workspace too small");
+    VT_REQUIRE(((uintptr_t)nodes & 255u) == 0 && ((uintptr_t)workspace & 255u) == 0,
+               "vt_bvh_build: buffers must be 256-byte aligned");
+    cudaStream_t s = (cudaStream_t)stream;
+    const uint32_t n = num_points;
+    char *w = (char *)workspace;
+    int *bb = (int *)w;
+    w += 256;
+    uint32_t *codes_in = (uint32_t *)w;  w += align256((size_t)n * 4);
+    uint32_t *codes_out = (uint32_t *)w; w += align256((size_t)n * 4);
+    uint32_t *ids_in = (uint32_t *)w;    w += align256((size_t)n * 4);
+    uint32_t *parent_leaf = (uint32_t *)w; w += align256((size_t)n * 4);
+    uint32_t *parent_int = (uint32_t *)w;  w += align256((size_t)n * 4);
+    uint32_t *flags = (uint32_t *)w;       w += align256((size_t)n * 4);
+    uint32_t *spare = (uint32_t *)w;       w += align256((size_t)n * 4);
+    (void)spare;
+    size_t temp_bytes = vt::bvh::sort_temp_bytes(n);
+    void *temp = w;
+    Node *nd = (Node *)nodes;
+    uint32_t *ids = (uint32_t *)((char *)nodes + align256((size_t)(n - 1) * sizeof(Node)));
+
+    vt::bvh::bbox_init<<<1, 32, 0, s>>>(bb);
+    unsigned g = vt::grid_for(n, 256);
+    vt::bvh::bbox_kernel<<<g < 1184 ? g : 1184, 256, 0, s>>>(points, n, bb);
+    vt::bvh::morton_kernel<<<g, 256, 0, s>>>(points, n, bb, codes_in, ids_in);
+    cudaError_t e = cub::DeviceRadixSort::SortPairs(temp, temp_bytes, codes_in, codes_out, ids_in,
+                                                    ids, (int)n, 0, 30, s);
+    if (e != cudaSuccess) return vt::set_error(VT_ERR_CUDA, "vt_bvh_build sort: %s", cudaGetErrorString(e));
+    if (n > 1) {
+        vt::bvh::karras_kernel<<<vt::grid_for(n - 1, 256), 256, 0, s>>>(codes_out, (int)n, nd,
+                                                                         parent_int, parent_leaf, flags);
+        vt::bvh::boxes_kernel<<<g, 256, 0, s>>>(points, (int)n, nd, ids, parent_int, parent_leaf,
+                                                flags);
+    }
+    return vt::check_launch("vt_bvh_build");
+}
+
+extern "C" vt_status vt_bvh_query(const void *nodes, const float *points, uint32_t num_points,
+                                  const float *queries, uint32_t num_queries, int32_t *out,
+                                  uint32_t *err, vt_stream stream)
+{
+    VT_REQUIRE(nodes && points && num_points > 0, "vt_bvh_query: BVH must be built before querying");
+    VT_REQUIRE(num_queries == 0 || (queries && out), "vt_bvh_query: null query buffers");
+    if (num_queries == 0) return VT_OK;
+    const Node *nd = (const Node *)nodes;
+    const uint32_t *ids =
+        (const uint32_t *)((const char *)nodes + align256((size_t)(num_points - 1) * sizeof(Node)));
+    vt::bvh::query_kernel<<<vt::grid_for(num_queries, 128), 128, 0, (cudaStream_t)stream>>>(
+        nd, ids, points, num_points, queries, num_queries, out, err);
+    return vt::check_launch("vt_bvh_query");
+}

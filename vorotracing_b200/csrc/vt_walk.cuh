@@ -1,0 +1,133 @@
+// vt_walk.cuh -- the cell-to-cell walk (reference: tracing_octmap.cu:39-123).
+//
+// Semantics are the reference's exactly: count the step, stop past
+// max_steps, pick the first face in CSR order with dp > 0 and the strictly
+// smallest bisector-plane distance t, stop when there is none, integrate the
+// segment [t0, t1] only when t1 > t0, and carry t0 = max(t0, t1).
+//
+// What differs is the schedule.  The reference walk has three dependent
+// global loads per cell (CSR offsets -> face offsets -> neighbour id ->
+// next offsets).  Here the packed 16-byte face record of the winning face
+// carries the neighbour id, its CSR begin and its degree, so the moment a
+// cell's exit face is known the walk issues the next cell's first face chunk,
+// its site and its density, and only then integrates the current segment
+// (texture loads included).  One dependent memory round trip per cell
+// remains, and the texture fetch overlaps it.  Face rows are read in chunks
+// of four 128-bit loads with the following chunk prefetched (double buffer).
+#pragma once
+
+#include "vt_geom.cuh"
+
+namespace vt {
+
+struct WalkDebug {
+    uint32_t *seq;      // (rays, seq_cap) visited cells, or null
+    uint32_t seq_cap;
+    uint32_t *seq_len;  // (rays) cells visited (may exceed seq_cap)
+    uint4 *stats;       // (rays) steps, faces tested, integrate calls, textured cells
+};
+
+struct FaceChunk {
+    uint4 f[4];
+};
+
+__device__ __forceinline__ void load_chunk(FaceChunk &c, const uint4 *__restrict__ row, uint32_t j,
+                                           uint32_t deg)
+{
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+        if (j + k < deg) c.f[k] = __ldg(row + j + k);
+}
+
+struct ExitFace {
+    float t1;
+    uint32_t nb, nbeg, ndeg;
+    bool found;
+};
+
+__device__ __forceinline__ void test_chunk(const FaceChunk &c, uint32_t j, uint32_t deg, V3 P,
+                                           const Ray &ray, ExitFace &x)
+{
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const uint4 f = c.f[k];
+        V3 off = mk(h2f((uint16_t)(f.x & 0xffffu)), h2f((uint16_t)(f.x >> 16)),
+                    h2f((uint16_t)(f.y & 0xffffu)));
+        V3 fo = P + 0.5f * off;
+        float dp = dot(off, ray.d);
+        float t = dot(fo - ray.o, off) / dp;
+        if (j + k < deg && dp > 0.0f && t < x.t1) {
+            x.t1 = t;
+            x.nb = f.z;
+            x.nbeg = f.w;
+            x.ndeg = f.y >> 16;
+            x.found = true;
+        }
+    }
+}
+
+// Integ must provide: bool integrate(uint32_t cell, float t0, float t1,
+//                                    V3 P, V3 Q, float density) and
+//                     uint32_t textured() const.
+template <class Integ, bool kDebug>
+__device__ __forceinline__ uint32_t walk(const Ray &ray, const uint4 *__restrict__ faces,
+                                         const uint32_t *__restrict__ offs,
+                                         const float *__restrict__ points,
+                                         const float *__restrict__ density, uint32_t start,
+                                         uint32_t max_steps, Integ &I, uint32_t ray_id,
+                                         const WalkDebug &dbg)
+{
+    uint32_t cur = start;
+    uint32_t begin = __ldg(offs + cur);
+    uint32_t deg = __ldg(offs + cur + 1) - begin;
+    V3 P = ld3(points + (size_t)cur * 3);
+    float s = __ldg(density + cur);
+    FaceChunk c;
+    load_chunk(c, faces + begin, 0, deg);
+
+    float t0 = 0.0f;
+    uint32_t n = 0;
+    uint32_t ns = 0, nfaces = 0, nint = 0;
+    for (;;) {
+        n++;
+        if (n > max_steps) break;
+        if (kDebug) {
+            if (dbg.seq && ns < dbg.seq_cap) dbg.seq[(size_t)ray_id * dbg.seq_cap + ns] = cur;
+            ns++;
+            nfaces += deg;
+        }
+        ExitFace x;
+        x.t1 = __int_as_float(0x7f800000);
+        x.found = false;
+        x.nb = x.nbeg = x.ndeg = 0;
+        const uint4 *row = faces + begin;
+        for (uint32_t j = 0; j < deg; j += 4) {
+            FaceChunk nxt;
+            load_chunk(nxt, row, j + 4, deg);
+            test_chunk(c, j, deg, P, ray, x);
+            c = nxt;
+        }
+        if (!x.found) break;
+        // Issue the next cell's loads before integrating this one.
+        V3 Q = ld3(points + (size_t)x.nb * 3);
+        float sn = __ldg(density + x.nb);
+        load_chunk(c, faces + x.nbeg, 0, x.ndeg);
+        if (x.t1 > t0) {
+            if (kDebug) nint++;
+            if (!I.integrate(cur, t0, x.t1, P, Q, s)) break;
+        }
+        t0 = fmaxf(t0, x.t1);
+        cur = x.nb;
+        P = Q;
+        s = sn;
+        begin = x.nbeg;
+        deg = x.ndeg;
+    }
+    if (kDebug) {
+        if (dbg.seq_len) dbg.seq_len[ray_id] = ns;
+        if (dbg.stats) dbg.stats[ray_id] = make_uint4(ns, nfaces, nint, I.textured());
+    }
+    return n;
+}
+
+}  // namespace vt

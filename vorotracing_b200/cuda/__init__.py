@@ -1,0 +1,15 @@
+"""Drop-in replacement for the reference's ``vorotracing.cuda`` operator module
+(vorotracing/cuda/__init__.py:49-57): same names, argument meaning, tensor
+layouts and error behaviour, backed by the sm_100a kernels of
+libvorotracing_b200.so."""
+from ._wrapper import (
+    prefetch_octmap_adj,
+    trace_octmap_infer,
+    trace_octmap_infer_q8,
+)
+
+__all__ = [
+    "trace_octmap_infer",
+    "trace_octmap_infer_q8",
+    "prefetch_octmap_adj",
+]

@@ -1,0 +1,224 @@
+"""Host-side operators over the C ABI, mirroring the reference's ``_C`` ops.
+
+Argument meaning, dtype rules and error messages follow the reference's
+validations (vorotracing/cuda/csrc/tracing/validations.h:17-66 and the ASSERTs
+of tracing_octmap.cu).  Outputs are allocated with torch on the rays' device
+and every kernel is launched on torch's current stream.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import torch
+
+from .. import _lib
+from .._lib import check, lib, ptr, stream_ptr
+
+FACE_ROW_HALVES = 8  # one packed face row = 16 bytes = 8 binary16
+
+
+def _fail(msg: str):
+    raise RuntimeError(msg)
+
+
+def validate_scene_data(points, attributes, adjacency, offsets):
+    """validations.h:17-66, same messages."""
+    if points.size(-1) != 3:
+        _fail(f"points had dimension {points.size(-1)} along axis -1, expected 3")
+    if points.dtype != torch.float32:
+        _fail(f"points had dtype {str(points.dtype).replace('torch.', '')}, expected float32")
+    if points.device.type != "cuda":
+        _fail("points must be on CUDA device")
+    n = points.numel() // 3
+    if attributes.device.type != "cuda":
+        _fail("attributes must be on CUDA device")
+    if offsets.dtype != torch.uint32:
+        _fail("point_adjacency_offsets must have uint32 dtype")
+    if offsets.device.type != "cuda":
+        _fail("point_adjacency_offsets must be on CUDA device")
+    if offsets.numel() != n + 1:
+        _fail("point_adjacency_offsets must have num_points + 1 elements")
+    if adjacency.dtype != torch.uint32:
+        _fail("point_adjacency must have uint32 dtype")
+    if adjacency.device.type != "cuda":
+        _fail("point_adjacency must be on CUDA device")
+
+
+def _aligned(t: torch.Tensor, align: int) -> torch.Tensor:
+    t = t.contiguous()
+    if t.numel() and t.data_ptr() % align:
+        t = t.clone()
+    return t
+
+
+def prefetch_faces(points, adjacency, offsets) -> torch.Tensor:
+    """Packed face rows (E_total + 4, 8) binary16, 16 bytes per CSR entry.
+
+    Replaces trace_vorotracing_prefetch_adj (tracing_octmap.cu:612-640); the
+    result is an opaque scene layout consumed by the trace operators."""
+    points = points.contiguous()
+    adjacency = adjacency.contiguous()
+    offsets = offsets.contiguous()
+    n = points.size(0)
+    e = adjacency.numel()
+    rows = int(lib().vt_face_rows(C.c_uint64(e)))
+    faces = torch.empty((rows, FACE_ROW_HALVES), dtype=torch.float16, device=points.device)
+    err = torch.zeros(1, dtype=torch.int32, device=points.device)
+    check(lib().vt_prefetch_adj(ptr(points), C.c_uint32(n), ptr(adjacency), C.c_uint64(e),
+                                ptr(offsets), C.c_uint64(e), ptr(faces), C.c_uint64(rows),
+                                ptr(err), stream_ptr(points.device)), "vt_prefetch_adj")
+    if int(err.item()) != 0:
+        _fail("invalid Voronoi adjacency: neighbour index out of range, offsets not monotone "
+              "or a cell degree above 65535")
+    return faces
+
+
+def make_scene(points, density, offsets, faces) -> _lib.VtScene:
+    return _lib.VtScene(points.data_ptr(), density.data_ptr(), offsets.data_ptr(),
+                        faces.data_ptr(), points.size(0), faces.size(0))
+
+
+def _check_faces(faces, adjacency, points):
+    if (faces.dtype != torch.float16 or faces.dim() != 2 or faces.size(1) != FACE_ROW_HALVES
+            or faces.size(0) < adjacency.numel()):
+        _fail("adjacent_diff must be the packed face tensor returned by prefetch_octmap_adj "
+              "of this package for the same adjacency")
+    if faces.device != points.device:
+        _fail("adjacent_diff must be on the points' device")
+
+
+def _check_err(err):
+    if int(err.item()) != 0:
+        _fail("trace: invalid start point or ray permutation index (out of range)")
+
+
+def _res_from(attr: torch.Tensor, channels: int) -> int:
+    per = attr.size(1) // channels
+    r = int(round(per ** 0.5))
+    if r * r * channels != attr.size(1) or r not in (4, 8):
+        _fail(f"octahedral texture rows must hold {channels}*R*R values with R in (4, 8), "
+              f"got {attr.size(1)}")
+    return r
+
+
+def trace_vorotracing_infer(points, diffuse, specular, density, adjacency, offsets, rays,
+                            start_point, adjacent_diff, ray_perm, weight_threshold: float,
+                            max_intersections: int, cell_skip_threshold: float,
+                            debug: dict | None = None):
+    """fp16 inference (tracing_octmap.cu:642-717).  Returns rgba (..., 4) float16."""
+    points = points.contiguous()
+    diffuse = _aligned(diffuse, 8)
+    specular = _aligned(specular, 8)
+    density = density.contiguous()
+    adjacency = adjacency.contiguous()
+    offsets = offsets.contiguous()
+    rays = _aligned(rays, 8)
+    start_point = start_point.contiguous()
+    validate_scene_data(points, diffuse, adjacency, offsets)
+    if diffuse.dtype != torch.float16:
+        _fail("inference kernel requires float16 diffuse")
+    if specular.dtype != torch.float16:
+        _fail("inference kernel requires float16 specular")
+    if density.dtype != torch.float32:
+        _fail("density must have float32 dtype")
+    if rays.dtype != torch.float32:
+        _fail("rays must have float32 dtype")
+    if start_point.dtype != torch.uint32:
+        _fail("start_point must have uint32 dtype")
+    return _infer_common(points, diffuse, specular, density, adjacency, offsets, rays,
+                         start_point, adjacent_diff, ray_perm, weight_threshold,
+                         max_intersections, cell_skip_threshold, None, debug)
+
+
+def trace_vorotracing_infer_q8(points, diffuse, specular, density, adjacency, offsets, rays,
+                               start_point, adjacent_diff, diff_scale, diff_offset, spec_scale,
+                               spec_offset, weight_threshold: float, max_intersections: int,
+                               cell_skip_threshold: float, ray_perm=None,
+                               debug: dict | None = None):
+    """q8 inference (tracing_octmap.cu:781-854).  Returns rgba (..., 4) float16."""
+    points = points.contiguous()
+    diffuse = diffuse.contiguous()
+    specular = specular.contiguous()
+    density = density.contiguous()
+    adjacency = adjacency.contiguous()
+    offsets = offsets.contiguous()
+    rays = _aligned(rays, 8)
+    start_point = start_point.contiguous()
+    validate_scene_data(points, diffuse, adjacency, offsets)
+    if diffuse.dtype != torch.uint8:
+        _fail("q8 inference kernel requires uint8 diffuse")
+    if specular.dtype != torch.uint8:
+        _fail("q8 inference kernel requires uint8 specular")
+    q8 = (float(diff_scale), float(diff_offset), float(spec_scale), float(spec_offset))
+    return _infer_common(points, diffuse, specular, density, adjacency, offsets, rays,
+                         start_point, adjacent_diff, ray_perm, weight_threshold,
+                         max_intersections, cell_skip_threshold, q8, debug)
+
+
+def _infer_common(points, diffuse, specular, density, adjacency, offsets, rays, start_point,
+                  adjacent_diff, ray_perm, wt, max_int, skip, q8, debug):
+    if rays.size(-1) != 6:
+        _fail("rays must have 6 as the last dimension")
+    if rays.device.type != "cuda":
+        _fail("rays must be on CUDA device")
+    nr = rays.numel() // 6
+    if start_point.numel() != nr:
+        _fail("start_point must have the same batch size as rays")
+    n = points.size(0)
+    if diffuse.size(0) != n or specular.size(0) != n or density.numel() != n:
+        _fail("diffuse, specular, density must each have num_points rows")
+    _check_faces(adjacent_diff, adjacency, points)
+    res = _res_from(diffuse, 3 if q8 else 4)
+    if _res_from(specular, 3 if q8 else 4) != res:
+        _fail("diffuse and specular octahedral resolutions must match")
+    perm = None
+    if ray_perm is not None and ray_perm.numel():
+        perm = ray_perm.contiguous()
+        if perm.numel() != nr:
+            _fail("ray_perm must be empty or have one entry per ray")
+        if perm.dtype not in (torch.int32, torch.uint32):
+            _fail("ray_perm must have int32 or uint32 dtype")
+    rgba = torch.empty(tuple(rays.shape[:-1]) + (4,), dtype=torch.float16, device=rays.device)
+    err = torch.zeros(1, dtype=torch.int32, device=rays.device)
+    scene = make_scene(points, density, offsets, adjacent_diff)
+    dbg, keep = _debug_struct(debug, nr)
+    L = lib()
+    stream = stream_ptr(rays.device)
+    if q8 is None:
+        st = L.vt_trace_infer_f16(C.byref(scene), ptr(diffuse), ptr(specular), C.c_int(res),
+                                  ptr(rays), C.c_uint32(nr), ptr(start_point), ptr(perm),
+                                  C.c_float(wt), C.c_uint32(max_int), C.c_float(skip),
+                                  ptr(rgba), dbg, ptr(err), stream)
+    else:
+        st = L.vt_trace_infer_q8(C.byref(scene), ptr(diffuse), ptr(specular), C.c_int(res),
+                                 *[C.c_float(v) for v in q8], ptr(rays), C.c_uint32(nr),
+                                 ptr(start_point), ptr(perm), C.c_float(wt), C.c_uint32(max_int),
+                                 C.c_float(skip), ptr(rgba), dbg, ptr(err), stream)
+    check(st, "trace infer")
+    if debug is not None or _CHECK_ERRORS:
+        _check_err(err)
+    del keep
+    return rgba
+
+
+# Reading the device error word forces a host sync; it is skipped on the
+# default path of the inference operators (invalid indices then yield zero
+# pixels) and always done when diagnostics are requested.
+_CHECK_ERRORS = False
+
+
+def _debug_struct(debug, nr):
+    """Allocate the optional per-ray diagnostics requested in ``debug`` (a dict
+    that receives the tensors): keys seq_cap, stats, num_intersections."""
+    if debug is None:
+        return None, None
+    dev = torch.device("cuda", torch.cuda.current_device())
+    cap = int(debug.get("seq_cap", 0))
+    seq = torch.zeros((nr, cap), dtype=torch.int32, device=dev) if cap else None
+    seq_len = torch.zeros(nr, dtype=torch.int32, device=dev) if cap else None
+    stats = torch.zeros((nr, 4), dtype=torch.int32, device=dev)
+    nint = torch.zeros(nr, dtype=torch.int32, device=dev)
+    debug.update(seq=seq, seq_len=seq_len, stats=stats, num_intersections=nint)
+    d = _lib.VtDebug(seq.data_ptr() if cap else None, cap, seq_len.data_ptr() if cap else None,
+                     stats.data_ptr(), nint.data_ptr())
+    return C.byref(d), (d, seq, seq_len, stats, nint)
