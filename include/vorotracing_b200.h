@@ -71,6 +71,8 @@ typedef struct {
     uint32_t *seq_len;           /* (rays) cells visited */
     uint32_t *stats;             /* (rays, 4) steps, faces tested, segments, textured */
     uint32_t *num_intersections; /* (rays) walk step count as the reference returns it */
+    uint8_t *visited;            /* (N) set to 1 for every cell a ray visits */
+    uint8_t *textured;           /* (N) set to 1 for every cell whose texels are read */
 } vt_debug;
 
 /* ---- packed faces (replaces the reference's adj_diff half4 rows) ---- */
@@ -105,6 +107,40 @@ VT_API vt_status vt_trace_infer_q8(const vt_scene *scene, const uint8_t *diffuse
                             float weight_threshold, uint32_t max_intersections,
                             float cell_skip_threshold, void *rgba, const vt_debug *debug,
                             uint32_t *err, vt_stream stream);
+
+/* ---- training ---- */
+
+/* Training forward (attr_half = 0: f32 attributes and rgba; 1: binary16).
+ * diffuse/specular (N, 3*res*res).  depth_quantiles (num_rays, K) f32 or null
+ * (K = 0); quantile_depths / quantile_indices (num_rays, K) out, unfilled
+ * entries -1 / 0xffffffff.  contribution (N) in the attribute dtype,
+ * zero-initialised by the caller, or null.  distortion, W_total, S_total,
+ * t_far (num_rays) f32 out. */
+VT_API vt_status vt_trace_fwd(const vt_scene *scene, int attr_half, const void *diffuse,
+                              const void *specular, int res, const float *rays, uint32_t num_rays,
+                              const uint32_t *start, uint32_t num_quantiles,
+                              const float *depth_quantiles, float weight_threshold,
+                              uint32_t max_intersections, void *rgba, float *quantile_depths,
+                              uint32_t *quantile_indices, uint32_t *num_intersections,
+                              void *contribution, float *distortion, float *W_total,
+                              float *S_total, float *t_far, const vt_debug *debug, uint32_t *err,
+                              vt_stream stream);
+
+/* Training backward.  Gradient outputs must be zero-initialised by the
+ * caller: points_grad (N,3) f32, diffuse/specular_grad in the attribute
+ * dtype, density_grad (N) f32, point_error (N) attribute dtype or null
+ * (accumulated only when ray_error is given). */
+VT_API vt_status vt_trace_bwd(const vt_scene *scene, int attr_half, const void *diffuse,
+                              const void *specular, int res, const float *rays, uint32_t num_rays,
+                              const uint32_t *start, uint32_t num_quantiles,
+                              const float *depth_quantiles, const uint32_t *quantile_indices,
+                              const void *rgba, const void *rgba_grad, const float *depth_grad,
+                              const void *ray_error, float contribution_alpha_grad,
+                              const float *distortion, const float *distortion_grad,
+                              const float *W_total, const float *S_total, float weight_threshold,
+                              uint32_t max_intersections, float *points_grad, void *diffuse_grad,
+                              void *specular_grad, float *density_grad, void *point_error,
+                              uint32_t *err, vt_stream stream);
 
 /* ---- ray-origin cell lookup (nearest site) ---- */
 

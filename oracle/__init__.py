@@ -234,3 +234,24 @@ def f2h(x):
     y = np.empty(x.shape, np.uint16)
     lib().vto_f2h_array(_p(x), _p(y), C.c_uint64(x.size))
     return y
+
+
+# ---------------------------------------------------------------- reference layout helpers
+
+def pad_f16x4(a: np.ndarray, res: int) -> np.ndarray:
+    """(N, 3R^2) float -> (N, 4R^2) float16 with a zero 4th channel (the
+    reference's _pad_3to4, vorotracing.py:505-512)."""
+    n = a.shape[0]
+    t = a.reshape(n, res * res, 3).astype(np.float16)
+    out = np.zeros((n, res * res, 4), np.float16)
+    out[..., :3] = t
+    return out.reshape(n, 4 * res * res)
+
+
+def quantize_u8(a: np.ndarray):
+    """The reference's _quantize_to_uint8 (vorotracing.py:495-503) in numpy."""
+    vmin = float(a.min())
+    vmax = float(a.max())
+    scale = (vmax - vmin) / 255.0
+    q = np.clip(np.rint((a - np.float32(vmin)) / np.float32(scale)), 0, 255).astype(np.uint8)
+    return q, scale, vmin

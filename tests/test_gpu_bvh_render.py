@@ -1,0 +1,77 @@
+"""Start-cell BVH against the oracle's brute-force nearest site, and the
+end-to-end InferScene render (Morton reorder + BVH + tile order + trace)
+against the oracle on the original cell order."""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from tests.conftest import pad_f16x4, quantize_u8
+
+pytestmark = pytest.mark.gpu
+
+
+def _dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def test_bvh_matches_brute_force(c1_scene):
+    from vorotracing_b200.cuda import NNBVH
+
+    pts = c1_scene["points"]
+    rng = np.random.default_rng(7)
+    q = np.concatenate([rng.uniform(-3, 3, (20000, 3)), pts[:500], pts[:500] + 1e-4,
+                        rng.uniform(-50, 50, (100, 3))]).astype(np.float32)
+    b = NNBVH()
+    b.build(_dev(pts))
+    got = b.query(_dev(pts), _dev(q)).cpu().numpy()
+    np.testing.assert_array_equal(got, oracle.nn_query(pts, q))
+
+
+@pytest.mark.parametrize("n", [1, 2, 3, 33])
+def test_bvh_tiny_and_duplicates(n):
+    from vorotracing_b200.cuda import nearest_neighbor_bvh
+
+    rng = np.random.default_rng(n)
+    pts = rng.integers(0, 2, (n, 3)).astype(np.float32)  # duplicates for n > 8
+    q = rng.uniform(-1, 2, (257, 3)).astype(np.float32)
+    got = nearest_neighbor_bvh(_dev(pts), _dev(q)).cpu().numpy()
+    np.testing.assert_array_equal(got, oracle.nn_query(pts, q))
+
+
+@pytest.mark.parametrize("quant", ["fp16", "q8"])
+def test_infer_scene_matches_oracle(c1_scene, c1_rays, quant):
+    from vorotracing_b200.render import InferScene
+
+    s = c1_scene
+    res = s["res"]
+    scene = InferScene(_dev(s["points"]), _dev(s["density"]), _dev(s["adj"]), _dev(s["offs"]),
+                       _dev(s["diffuse"]), _dev(s["specular"]), quantize=quant, sort_morton=True)
+    rgba = scene.render(_dev(c1_rays), weight_threshold=0.01, cell_skip_threshold=1e-3)
+    torch.cuda.synchronize()
+    start = oracle.nn_query(s["points"], c1_rays.reshape(-1, 6)[:1, :3])
+    start = np.full(c1_rays.shape[0] * c1_rays.shape[1], start[0], np.uint32)
+    if quant == "fp16":
+        S = oracle.Scene(s["points"], s["adj"], s["offs"], s["density"],
+                         pad_f16x4(s["diffuse"], res), pad_f16x4(s["specular"], res),
+                         oracle.ATTR_F16X4)
+    else:
+        dq, ds, do = quantize_u8(s["diffuse"])
+        sq, ss, so = quantize_u8(s["specular"])
+        S = oracle.Scene(s["points"], s["adj"], s["offs"], s["density"], dq, sq, oracle.ATTR_U8,
+                         q8=(ds, do, ss, so))
+    ref = oracle.trace_infer(S, c1_rays, start, wt=0.01, skip=1e-3)
+    np.testing.assert_array_equal(rgba.reshape(-1, 4).cpu().numpy().view(np.uint16),
+                                  ref["rgba"].view(np.uint16))
+
+
+def test_render_host_roundtrip(c1_scene, c1_rays):
+    from vorotracing_b200.render import InferScene
+
+    s = c1_scene
+    scene = InferScene(_dev(s["points"]), _dev(s["density"]), _dev(s["adj"]), _dev(s["offs"]),
+                       _dev(s["diffuse"]), _dev(s["specular"]))
+    host = torch.from_numpy(c1_rays).pin_memory()
+    out = scene.render_host(host, weight_threshold=0.01)
+    dev = scene.render(_dev(c1_rays), weight_threshold=0.01).cpu()
+    assert torch.equal(out.view(torch.int16), dev.view(torch.int16))

@@ -22,7 +22,8 @@ class VtScene(C.Structure):
 
 class VtDebug(C.Structure):
     _fields_ = [("seq", C.c_void_p), ("seq_cap", C.c_uint32), ("seq_len", C.c_void_p),
-                ("stats", C.c_void_p), ("num_intersections", C.c_void_p)]
+                ("stats", C.c_void_p), ("num_intersections", C.c_void_p),
+                ("visited", C.c_void_p), ("textured", C.c_void_p)]
 
 
 def lib():

@@ -95,10 +95,11 @@ vt_status fill_args(InferArgs &a, const vt_scene *scene, const float *rays, uint
     a.skip = skip;
     a.max_steps = max_int;
     a.rgba = (uint2 *)rgba;
-    a.dbg = WalkDebug{nullptr, 0, nullptr, nullptr};
+    a.dbg = WalkDebug{nullptr, 0, nullptr, nullptr, nullptr, nullptr};
     a.n_out = nullptr;
     if (dbg) {
-        a.dbg = WalkDebug{dbg->seq, dbg->seq_cap, dbg->seq_len, (uint4 *)dbg->stats};
+        a.dbg = WalkDebug{dbg->seq, dbg->seq_cap, dbg->seq_len, (uint4 *)dbg->stats,
+                          dbg->visited, dbg->textured};
         a.n_out = dbg->num_intersections;
         VT_REQUIRE(((uintptr_t)dbg->stats & 15u) == 0, "%s: stats must be 16-byte aligned", who);
     }

@@ -1,0 +1,277 @@
+// vt_train.cu -- training forward / backward kernels and C entry points
+// (reference kernels tracing_octmap.cu:151-230 and :232-340, host wrappers
+// :355-546 and :860-1103).  One thread per ray, rays in input order.  The
+// packed face rows replace the reference's per-call adj_diff prefetch; the
+// host layer rebuilds them from the current sites before each call, as the
+// reference re-runs its prefetch kernel on every fwd / bwd call.
+#include "vt_abi.cuh"
+#include "vt_train_integ.cuh"
+#include "vt_walk.cuh"
+
+namespace vt {
+
+constexpr int kTrainBlock = 128;
+
+struct TrainCommon {
+    const float *points;
+    const float *density;
+    const uint32_t *offs;
+    const uint4 *faces;
+    uint32_t n_points;
+    const float *rays;
+    uint32_t num_rays;
+    const uint32_t *start;
+    uint32_t K;
+    const float *dq;
+    float wt;
+    uint32_t max_steps;
+    uint32_t *err;
+};
+
+template <class AT> struct FwdOut {
+    AT *rgba;
+    float *qdepth;
+    uint32_t *qidx;
+    uint32_t *n_int;
+    AT *contrib;
+    float *dist, *W, *S, *tfar;
+    WalkDebug dbg;
+};
+
+template <class AT, int R, bool kDebug>
+__global__ void __launch_bounds__(kTrainBlock)
+    fwd_kernel(TrainCommon a, TexPlain<AT, R> tex, FwdOut<AT> o)
+{
+    uint32_t r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= a.num_rays) return;
+    Ray ray = load_ray(a.rays, r);
+    uint32_t start = __ldg(a.start + r);
+    const float *qthr = a.dq ? a.dq + (size_t)r * a.K : nullptr;
+    float *qd = o.qdepth ? o.qdepth + (size_t)r * a.K : nullptr;
+    uint32_t *qi = o.qidx ? o.qidx + (size_t)r * a.K : nullptr;
+    FwdInteg<AT, R> I(ray, tex, a.wt, qthr, a.dq ? a.K : 0, qd, qi, o.contrib);
+    uint32_t n = 0;
+    if (start < a.n_points)
+        n = walk<FwdInteg<AT, R>, kDebug>(ray, a.faces, a.offs, a.points, a.density, start,
+                                          a.max_steps, I, r, o.dbg);
+    else
+        report(a.err, VT_ERR_DATA);
+    for (uint32_t i = I.qi; i < a.K; ++i) {
+        qd[i] = -1.0f;
+        qi[i] = 0xffffffffu;
+    }
+    AT *out = o.rgba + (size_t)r * 4;
+    out[0] = fromf<AT>(I.acc.x);
+    out[1] = fromf<AT>(I.acc.y);
+    out[2] = fromf<AT>(I.acc.z);
+    out[3] = fromf<AT>(1.0f - I.T);
+    if (o.n_int) o.n_int[r] = n;
+    o.dist[r] = 2.0f * I.dist + I.self / 3.0f;
+    o.W[r] = I.W;
+    o.S[r] = I.S;
+    o.tfar[r] = I.tfar;
+}
+
+template <class AT> struct BwdIn {
+    const uint32_t *qidx;
+    const AT *rgba;
+    const AT *rgba_grad;
+    const float *depth_grad;
+    const AT *ray_error;
+    float contribution_alpha_grad;
+    const float *dist, *dist_grad, *W, *S;
+    float *points_grad;
+    AT *diffuse_grad, *specular_grad;
+    float *density_grad;
+    AT *point_error;
+};
+
+template <class AT, int R>
+__global__ void __launch_bounds__(kTrainBlock)
+    bwd_kernel(TrainCommon a, TexPlain<AT, R> tex, BwdIn<AT> b)
+{
+    uint32_t r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= a.num_rays) return;
+    Ray ray = load_ray(a.rays, r);
+    uint32_t start = __ldg(a.start + r);
+    if (start >= a.n_points) {
+        report(a.err, VT_ERR_DATA);
+        return;
+    }
+    BwdInteg<AT, R> I;
+    I.ray = ray;
+    I.tex = tex;
+    I.wt = a.wt;
+    I.acc = mk(0.f, 0.f, 0.f);
+    I.T = 1.0f;
+    I.ntex = 0;
+    float c[4], g[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        c[k] = tof<AT>(b.rgba[(size_t)r * 4 + k]);
+        g[k] = tof<AT>(b.rgba_grad[(size_t)r * 4 + k]);
+    }
+    g[3] += b.contribution_alpha_grad;
+    I.fwd_rgb = mk(c[0], c[1], c[2]);
+    I.fwd_a = c[3];
+    I.g_rgb = mk(g[0], g[1], g[2]);
+    I.g_a = g[3];
+    I.ray_error = b.ray_error ? tof<AT>(b.ray_error[r]) : 0.0f;
+    float cdg = 0.0f;
+    for (uint32_t i = 0; i < a.K; ++i) {
+        uint32_t pi = b.qidx[(size_t)r * a.K + i];
+        if (pi != 0xffffffffu) cdg += b.depth_grad[(size_t)r * a.K + i] / __ldg(a.density + pi);
+    }
+    I.cur_dg = cdg;
+    I.K = a.dq ? a.K : 0;
+    I.qthr = a.dq ? a.dq + (size_t)r * a.K : nullptr;
+    I.dgrad = b.depth_grad ? b.depth_grad + (size_t)r * a.K : nullptr;
+    I.qi = 0;
+    I.qv = I.K > 0 ? I.qthr[0] : 0.0f;
+    I.W = 0.f;
+    I.S = 0.f;
+    I.Wt = b.W ? b.W[r] : 0.0f;
+    I.St = b.S ? b.S[r] : 0.0f;
+    float fd = b.dist ? b.dist[r] : 0.0f;
+    I.dgr = b.dist_grad ? b.dist_grad[r] : 0.0f;
+    I.Dt = (2.0f * fd) * I.dgr;
+    I.Drun = 0.0f;
+    I.pgrad = b.points_grad;
+    I.ddiff = b.diffuse_grad;
+    I.dspec = b.specular_grad;
+    I.dden = b.density_grad;
+    I.perr = b.point_error;
+    I.prev_geom = I.prev_grad = I.cur_grad = I.next_grad = mk(0.f, 0.f, 0.f);
+    I.prev_idx = 0xffffffffu;
+    float tu, tv;
+    oct_encode<R>(mk(-ray.d.x, -ray.d.y, -ray.d.z), tu, tv);
+    I.spec = make_bilin<R>(tu, tv);
+    WalkDebug none{nullptr, 0, nullptr, nullptr, nullptr, nullptr};
+    walk<BwdInteg<AT, R>, false>(ray, a.faces, a.offs, a.points, a.density, start, a.max_steps, I,
+                                 r, none);
+}
+
+vt_status fill_common(TrainCommon &a, const vt_scene *scene, const float *rays, uint32_t nr,
+                      const uint32_t *start, uint32_t K, const float *dq, float wt,
+                      uint32_t max_int, uint32_t *err, const char *who)
+{
+    VT_REQUIRE(scene && scene->points && scene->density && scene->offsets && scene->faces,
+               "%s: incomplete scene", who);
+    VT_REQUIRE(scene->num_points > 0, "%s: empty scene", who);
+    VT_REQUIRE(((uintptr_t)scene->faces & 15u) == 0, "%s: faces must be 16-byte aligned", who);
+    VT_REQUIRE(nr == 0 || (rays && start), "%s: null ray buffers", who);
+    VT_REQUIRE(((uintptr_t)rays & 7u) == 0, "%s: rays must be 8-byte aligned", who);
+    VT_REQUIRE(K == 0 || dq, "%s: depth quantiles missing", who);
+    a = TrainCommon{scene->points, scene->density, scene->offsets, (const uint4 *)scene->faces,
+                    scene->num_points, rays, nr, start, K, dq, wt, max_int, err};
+    return VT_OK;
+}
+
+template <class AT, int R>
+vt_status launch_fwd(const TrainCommon &a, const void *dif, const void *spe, const FwdOut<AT> &o,
+                     bool debug, cudaStream_t s)
+{
+    TexPlain<AT, R> t{(const AT *)dif, (const AT *)spe};
+    unsigned g = grid_for(a.num_rays, kTrainBlock);
+    if (debug)
+        fwd_kernel<AT, R, true><<<g, kTrainBlock, 0, s>>>(a, t, o);
+    else
+        fwd_kernel<AT, R, false><<<g, kTrainBlock, 0, s>>>(a, t, o);
+    return check_launch("fwd_kernel");
+}
+
+template <class AT, int R>
+vt_status launch_bwd(const TrainCommon &a, const void *dif, const void *spe, const BwdIn<AT> &b,
+                     cudaStream_t s)
+{
+    TexPlain<AT, R> t{(const AT *)dif, (const AT *)spe};
+    bwd_kernel<AT, R><<<grid_for(a.num_rays, kTrainBlock), kTrainBlock, 0, s>>>(a, t, b);
+    return check_launch("bwd_kernel");
+}
+
+}  // namespace vt
+
+extern "C" vt_status vt_trace_fwd(const vt_scene *scene, int attr_half, const void *diffuse,
+                                  const void *specular, int res, const float *rays,
+                                  uint32_t num_rays, const uint32_t *start,
+                                  uint32_t num_quantiles, const float *depth_quantiles,
+                                  float weight_threshold, uint32_t max_intersections, void *rgba,
+                                  float *quantile_depths, uint32_t *quantile_indices,
+                                  uint32_t *num_intersections, void *contribution,
+                                  float *distortion, float *W_total, float *S_total, float *t_far,
+                                  const vt_debug *debug, uint32_t *err, vt_stream stream)
+{
+    vt::TrainCommon a;
+    vt_status st = vt::fill_common(a, scene, rays, num_rays, start, num_quantiles, depth_quantiles,
+                                   weight_threshold, max_intersections, err, "vt_trace_fwd");
+    if (st != VT_OK) return st;
+    VT_REQUIRE(diffuse && specular, "vt_trace_fwd: null textures");
+    VT_REQUIRE(num_rays == 0 || (rgba && distortion && W_total && S_total && t_far),
+               "vt_trace_fwd: null outputs");
+    VT_REQUIRE(num_quantiles == 0 || (quantile_depths && quantile_indices),
+               "vt_trace_fwd: null depth outputs");
+    if (num_rays == 0) return VT_OK;
+    vt::WalkDebug dbg{nullptr, 0, nullptr, nullptr, nullptr, nullptr};
+    if (debug)
+        dbg = vt::WalkDebug{debug->seq, debug->seq_cap, debug->seq_len, (uint4 *)debug->stats,
+                            debug->visited, debug->textured};
+    cudaStream_t s = (cudaStream_t)stream;
+    if (attr_half) {
+        vt::FwdOut<__half> o{(__half *)rgba, quantile_depths, quantile_indices, num_intersections,
+                             (__half *)contribution, distortion, W_total, S_total, t_far, dbg};
+        if (res == 8) return vt::launch_fwd<__half, 8>(a, diffuse, specular, o, debug, s);
+        if (res == 4) return vt::launch_fwd<__half, 4>(a, diffuse, specular, o, debug, s);
+    } else {
+        vt::FwdOut<float> o{(float *)rgba, quantile_depths, quantile_indices, num_intersections,
+                            (float *)contribution, distortion, W_total, S_total, t_far, dbg};
+        if (res == 8) return vt::launch_fwd<float, 8>(a, diffuse, specular, o, debug, s);
+        if (res == 4) return vt::launch_fwd<float, 4>(a, diffuse, specular, o, debug, s);
+    }
+    return vt::set_error(VT_ERR_INVALID, "vt_trace_fwd: res must be 4 or 8, got %d", res);
+}
+
+extern "C" vt_status vt_trace_bwd(const vt_scene *scene, int attr_half, const void *diffuse,
+                                  const void *specular, int res, const float *rays,
+                                  uint32_t num_rays, const uint32_t *start,
+                                  uint32_t num_quantiles, const float *depth_quantiles,
+                                  const uint32_t *quantile_indices, const void *rgba,
+                                  const void *rgba_grad, const float *depth_grad,
+                                  const void *ray_error, float contribution_alpha_grad,
+                                  const float *distortion, const float *distortion_grad,
+                                  const float *W_total, const float *S_total,
+                                  float weight_threshold, uint32_t max_intersections,
+                                  float *points_grad, void *diffuse_grad, void *specular_grad,
+                                  float *density_grad, void *point_error, uint32_t *err,
+                                  vt_stream stream)
+{
+    vt::TrainCommon a;
+    vt_status st = vt::fill_common(a, scene, rays, num_rays, start, num_quantiles, depth_quantiles,
+                                   weight_threshold, max_intersections, err, "vt_trace_bwd");
+    if (st != VT_OK) return st;
+    VT_REQUIRE(diffuse && specular, "vt_trace_bwd: null textures");
+    VT_REQUIRE(num_rays == 0 || (rgba && rgba_grad), "vt_trace_bwd: null rgba inputs");
+    VT_REQUIRE(points_grad && diffuse_grad && specular_grad && density_grad,
+               "vt_trace_bwd: null gradient outputs");
+    VT_REQUIRE(num_quantiles == 0 || (quantile_indices && depth_grad),
+               "vt_trace_bwd: depth_grad must be provided if depth_quantiles is provided");
+    if (num_rays == 0) return VT_OK;
+    cudaStream_t s = (cudaStream_t)stream;
+    if (attr_half) {
+        vt::BwdIn<__half> b{quantile_indices, (const __half *)rgba, (const __half *)rgba_grad,
+                            depth_grad, (const __half *)ray_error, contribution_alpha_grad,
+                            distortion, distortion_grad, W_total, S_total, points_grad,
+                            (__half *)diffuse_grad, (__half *)specular_grad, density_grad,
+                            (__half *)point_error};
+        if (res == 8) return vt::launch_bwd<__half, 8>(a, diffuse, specular, b, s);
+        if (res == 4) return vt::launch_bwd<__half, 4>(a, diffuse, specular, b, s);
+    } else {
+        vt::BwdIn<float> b{quantile_indices, (const float *)rgba, (const float *)rgba_grad,
+                           depth_grad, (const float *)ray_error, contribution_alpha_grad,
+                           distortion, distortion_grad, W_total, S_total, points_grad,
+                           (float *)diffuse_grad, (float *)specular_grad, density_grad,
+                           (float *)point_error};
+        if (res == 8) return vt::launch_bwd<float, 8>(a, diffuse, specular, b, s);
+        if (res == 4) return vt::launch_bwd<float, 4>(a, diffuse, specular, b, s);
+    }
+    return vt::set_error(VT_ERR_INVALID, "vt_trace_bwd: res must be 4 or 8, got %d", res);
+}

@@ -1,0 +1,272 @@
+// vt_train_integ.cuh -- training integrators (fp32 or fp16 attributes, layout
+// (N, 3*R*R) with texel t channel c at t*3 + c).
+//
+//   FwdInteg  ray_integrator_octmap.cuh:57-282: colour only for density > 1e-6
+//             but T always advances; mip-NeRF 360 distortion accumulators in
+//             s = 1 - 1/(1+t) space; optional per-cell contribution; depth at
+//             the transmittance quantiles; continue while T > weight_threshold.
+//   BwdInteg  ray_integrator_octmap.cuh:635-1027: replays the forward and
+//             scatters gradients; site gradients through the bisector-plane
+//             geometry are flushed one cell late; the walk stops (and flushes
+//             the pending site gradient) only when T < weight_threshold.
+#pragma once
+
+#include "vt_geom.cuh"
+
+namespace vt {
+
+template <class AT> __device__ __forceinline__ float tof(AT v);
+template <> __device__ __forceinline__ float tof<float>(float v) { return v; }
+template <> __device__ __forceinline__ float tof<__half>(__half v) { return __half2float(v); }
+template <class AT> __device__ __forceinline__ AT fromf(float v);
+template <> __device__ __forceinline__ float fromf<float>(float v) { return v; }
+template <> __device__ __forceinline__ __half fromf<__half>(float v) { return __float2half_rn(v); }
+
+template <class AT> __device__ __forceinline__ void atomic_add(AT *p, float v);
+template <> __device__ __forceinline__ void atomic_add<float>(float *p, float v) { atomicAdd(p, v); }
+template <> __device__ __forceinline__ void atomic_add<__half>(__half *p, float v)
+{
+    atomicAdd(p, __float2half_rn(v));
+}
+
+template <class AT, int R> struct TexPlain {
+    const AT *diffuse;
+    const AT *specular;
+    __device__ __forceinline__ V3 logits(uint32_t cell, const Bilin &d, const Bilin &s) const
+    {
+        const AT *dp = diffuse + (size_t)cell * (3 * R * R);
+        const AT *sp = specular + (size_t)cell * (3 * R * R);
+        float a[4][3], b[4][3];
+        const int di[4] = {d.i00, d.i10, d.i01, d.i11};
+        const int si[4] = {s.i00, s.i10, s.i01, s.i11};
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+#pragma unroll
+            for (int c = 0; c < 3; ++c) {
+                a[k][c] = tof<AT>(dp[di[k] * 3 + c]);
+                b[k][c] = tof<AT>(sp[si[k] * 3 + c]);
+            }
+        float r[3];
+#pragma unroll
+        for (int c = 0; c < 3; ++c)
+            r[c] = blend(d, a[0][c], a[1][c], a[2][c], a[3][c]) +
+                   blend(s, b[0][c], b[1][c], b[2][c], b[3][c]);
+        return mk(r[0], r[1], r[2]);
+    }
+};
+
+template <class AT, int R> struct FwdInteg {
+    Ray ray;
+    TexPlain<AT, R> tex;
+    Bilin spec;
+    float wt;
+    V3 acc;
+    float T;
+    uint32_t ntex;
+    const float *qthr;
+    uint32_t K, qi;
+    float qv;
+    float *qdepth;
+    uint32_t *qidx;
+    float W, S, dist, self, tfar;
+    AT *contrib;
+
+    __device__ __forceinline__ FwdInteg(const Ray &r, const TexPlain<AT, R> &t, float wt_,
+                                        const float *qthr_, uint32_t K_, float *qdepth_,
+                                        uint32_t *qidx_, AT *contrib_)
+        : ray(r), tex(t), wt(wt_), acc(mk(0.f, 0.f, 0.f)), T(1.0f), ntex(0), qthr(qthr_), K(K_),
+          qi(0), qv(0.0f), qdepth(qdepth_), qidx(qidx_), W(0.f), S(0.f), dist(0.f), self(0.f),
+          tfar(0.f), contrib(contrib_)
+    {
+        if (K > 0) qv = qthr[0];
+        float tu, tv;
+        oct_encode<R>(mk(-r.d.x, -r.d.y, -r.d.z), tu, tv);
+        spec = make_bilin<R>(tu, tv);
+    }
+
+    __device__ __forceinline__ uint32_t textured() const { return ntex; }
+
+    __device__ __forceinline__ bool integrate(uint32_t cell, float t0, float t1, V3 P, V3, float s)
+    {
+        V3 rgb = mk(0.f, 0.f, 0.f);
+        if (s > 1e-6f) {
+            float tu, tv;
+            oct_encode<R>(probe_dir(ray, t0, P), tu, tv);
+            Bilin d = make_bilin<R>(tu, tv);
+            V3 l = tex.logits(cell, d, spec);
+            rgb = mk(sigmoid(l.x), sigmoid(l.y), sigmoid(l.z));
+            ntex++;
+        }
+        float delta = fmaxf(t1 - t0, 0.0f);
+        float alpha = 1.0f - expf_exact(-s * delta);
+        float w = T * alpha;
+        float s0 = 1.0f - 1.0f / (1.0f + t0);
+        float s1 = 1.0f - 1.0f / (1.0f + t1);
+        float mid = 0.5f * (s0 + s1);
+        float ds = s1 - s0;
+        dist += w * (mid * W - S);
+        self += (w * w) * ds;
+        W += w;
+        S += w * mid;
+        if (t1 > tfar) tfar = t1;
+        if (contrib) atomic_add<AT>(contrib + cell, w);
+        acc = acc + w * rgb;
+        float nT = T * (1.0f - alpha);
+        while (qi < K && nT < qv) {
+            qdepth[qi] = t0 + logf_exact(T / qv) / s;
+            qidx[qi] = cell;
+            qi++;
+            if (qi < K) qv = qthr[qi];
+        }
+        T = nT;
+        return T > wt;
+    }
+};
+
+// d t / d site for the bisector-plane hit (ray_integrator.cuh:39-53).
+__device__ __forceinline__ V3 cig(V3 p, V3 q, const Ray &ray)
+{
+    V3 fo = 0.5f * (p + q);
+    V3 n = q - p;
+    float num = dot(fo - ray.o, n);
+    float dp = dot(n, ray.d);
+    V3 g = num * ray.d + dp * (ray.o - p);
+    return divs(g, dp * dp);
+}
+
+__device__ __forceinline__ void atomic_add3(float *p, V3 v)
+{
+    atomicAdd(p, v.x);
+    atomicAdd(p + 1, v.y);
+    atomicAdd(p + 2, v.z);
+}
+
+template <class AT, int R> struct BwdInteg {
+    Ray ray;
+    TexPlain<AT, R> tex;
+    Bilin spec;
+    float wt;
+    V3 acc;
+    float T;
+    uint32_t ntex;
+    V3 fwd_rgb, g_rgb;
+    float fwd_a, g_a;
+    const float *qthr;
+    const float *dgrad;
+    uint32_t K, qi;
+    float qv, cur_dg, ray_error;
+    float W, S, Wt, St, dgr, Dt, Drun;
+    float *pgrad;
+    AT *ddiff, *dspec;
+    float *dden;
+    AT *perr;
+    V3 prev_geom, prev_grad, cur_grad, next_grad;
+    uint32_t prev_idx;
+
+    __device__ __forceinline__ uint32_t textured() const { return ntex; }
+
+    __device__ __forceinline__ void scatter(AT *g, uint32_t cell, const Bilin &b, V3 dl) const
+    {
+        AT *base = g + (size_t)cell * (3 * R * R);
+        const float d[3] = {dl.x, dl.y, dl.z};
+#pragma unroll
+        for (int c = 0; c < 3; ++c) {
+            atomic_add<AT>(base + b.i00 * 3 + c, b.w00 * d[c]);
+            atomic_add<AT>(base + b.i10 * 3 + c, b.w10 * d[c]);
+            atomic_add<AT>(base + b.i01 * 3 + c, b.w01 * d[c]);
+            atomic_add<AT>(base + b.i11 * 3 + c, b.w11 * d[c]);
+        }
+    }
+
+    __device__ __forceinline__ bool integrate(uint32_t cell, float t0, float t1, V3 P, V3 Q, float s)
+    {
+        V3 rgb = mk(0.f, 0.f, 0.f);
+        Bilin db;
+        bool has_color = false;
+        if (s > 1e-6f) {
+            float tu, tv;
+            oct_encode<R>(probe_dir(ray, t0, P), tu, tv);
+            db = make_bilin<R>(tu, tv);
+            V3 l = tex.logits(cell, db, spec);
+            rgb = mk(sigmoid(l.x), sigmoid(l.y), sigmoid(l.z));
+            has_color = true;
+            ntex++;
+        }
+        float delta = fmaxf(t1 - t0, 0.0f);
+        float alpha = 1.0f - expf_exact(-s * delta);
+        float w = T * alpha;
+        float dads = delta * (1.0f - alpha);
+        float dadd = 0.0f;
+        if (delta > 0.0f) dadd = s * (1.0f - alpha);
+        acc = acc + w * rgb;
+        if (perr) atomic_add<AT>(perr + cell, w * ray_error);
+        V3 dLdrgb = mk(g_rgb.x * w, g_rgb.y * w, g_rgb.z * w);
+        V3 rest = divs(fwd_rgb - acc, T * ((1.0f - alpha) + 1e-6f));
+        float dLda = T * dot(rgb - rest, g_rgb);
+        dLda += ((1.0f - fwd_a) * g_a) / ((1.0f - alpha) + 1e-6f);
+        float dLds = dLda * dads;
+        float dLddt = dLda * dadd;
+        float dLdt0 = 0.0f;
+        if (dgr != 0.0f) {
+            float s0 = 1.0f - 1.0f / (1.0f + t0);
+            float s1 = 1.0f - 1.0f / (1.0f + t1);
+            float mid = 0.5f * (s0 + s1);
+            float ds = s1 - s0;
+            float Wm = W, Sm = S;
+            float Wp = (Wt - Wm) - w;
+            float Sp = (St - Sm) - w * mid;
+            float raw = (2.0f * (mid * Wm - Sm) + 2.0f * (Sp - mid * Wp)) + ((2.0f / 3.0f) * w) * ds;
+            float outer = raw * dgr;
+            float ww = outer * w;
+            float Dip = (Dt - Drun) - ww;
+            dLds += ((outer * T) * dads) - delta * Dip;
+            Drun += ww;
+            W += w;
+            S += w * mid;
+        }
+        float nT = T * (1.0f - alpha);
+        while (qi < K && nT < qv) {
+            float gi = dgrad[qi] / s;
+            dLdt0 += gi;
+            dLds += ((-gi) * logf_exact(T / qv)) / s;
+            cur_dg -= gi;
+            qi++;
+            if (qi < K) qv = qthr[qi];
+        }
+        if (qi < K) {
+            dLds += (-delta) * cur_dg;
+            dLddt += (-s) * cur_dg;
+        }
+        dLdt0 += -dLddt;
+        float dLdt1 = dLddt;
+        V3 g_prev = mk(0.f, 0.f, 0.f);
+        if (prev_idx != 0xffffffffu) g_prev = cig(prev_geom, P, ray);
+        V3 g1c = cig(P, Q, ray);
+        V3 g0c = cig(P, prev_geom, ray);
+        V3 g1n = cig(Q, P, ray);
+        prev_grad = prev_grad + dLdt0 * g_prev;
+        cur_grad = cur_grad + (dLdt0 * g0c + dLdt1 * g1c);
+        next_grad = next_grad + dLdt1 * g1n;
+        if (prev_idx != 0xffffffffu) atomic_add3(pgrad + (size_t)prev_idx * 3, prev_grad);
+        prev_geom = P;
+        prev_idx = cell;
+        prev_grad = cur_grad;
+        cur_grad = next_grad;
+        next_grad = mk(0.f, 0.f, 0.f);
+        T = nT;
+        if (has_color) {
+            V3 dl = mk((dLdrgb.x * rgb.x) * (1.0f - rgb.x), (dLdrgb.y * rgb.y) * (1.0f - rgb.y),
+                       (dLdrgb.z * rgb.z) * (1.0f - rgb.z));
+            scatter(ddiff, cell, db, dl);
+            scatter(dspec, cell, spec, dl);
+        }
+        atomicAdd(dden + cell, dLds);
+        if (T < wt) {
+            atomic_add3(pgrad + (size_t)prev_idx * 3, prev_grad);
+            return false;
+        }
+        return true;
+    }
+};
+
+}  // namespace vt

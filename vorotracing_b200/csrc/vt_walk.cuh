@@ -25,6 +25,8 @@ struct WalkDebug {
     uint32_t seq_cap;
     uint32_t *seq_len;  // (rays) cells visited (may exceed seq_cap)
     uint4 *stats;       // (rays) steps, faces tested, integrate calls, textured cells
+    uint8_t *visited;   // (cells) 1 if any ray visits the cell
+    uint8_t *textured;  // (cells) 1 if any ray reads the cell's texels
 };
 
 struct FaceChunk {
@@ -93,6 +95,7 @@ __device__ __forceinline__ uint32_t walk(const Ray &ray, const uint4 *__restrict
         if (n > max_steps) break;
         if (kDebug) {
             if (dbg.seq && ns < dbg.seq_cap) dbg.seq[(size_t)ray_id * dbg.seq_cap + ns] = cur;
+            if (dbg.visited) dbg.visited[cur] = 1;
             ns++;
             nfaces += deg;
         }
@@ -114,7 +117,10 @@ __device__ __forceinline__ uint32_t walk(const Ray &ray, const uint4 *__restrict
         load_chunk(c, faces + x.nbeg, 0, x.ndeg);
         if (x.t1 > t0) {
             if (kDebug) nint++;
-            if (!I.integrate(cur, t0, x.t1, P, Q, s)) break;
+            const uint32_t tex_before = kDebug ? I.textured() : 0;
+            const bool go = I.integrate(cur, t0, x.t1, P, Q, s);
+            if (kDebug && dbg.textured && I.textured() != tex_before) dbg.textured[cur] = 1;
+            if (!go) break;
         }
         t0 = fmaxf(t0, x.t1);
         cur = x.nb;

@@ -2,6 +2,7 @@
 (vorotracing/cuda/__init__.py:49-57): same names, argument meaning, tensor
 layouts and error behaviour, backed by the sm_100a kernels of
 libvorotracing_b200.so."""
+from ._ops import NNBVH, nearest_neighbor_bvh
 from ._wrapper import (
     prefetch_octmap_adj,
     trace_octmap_infer,
@@ -12,4 +13,6 @@ __all__ = [
     "trace_octmap_infer",
     "trace_octmap_infer_q8",
     "prefetch_octmap_adj",
+    "NNBVH",
+    "nearest_neighbor_bvh",
 ]

@@ -181,7 +181,7 @@ def _infer_common(points, diffuse, specular, density, adjacency, offsets, rays, 
     rgba = torch.empty(tuple(rays.shape[:-1]) + (4,), dtype=torch.float16, device=rays.device)
     err = torch.zeros(1, dtype=torch.int32, device=rays.device)
     scene = make_scene(points, density, offsets, adjacent_diff)
-    dbg, keep = _debug_struct(debug, nr)
+    dbg, keep = _debug_struct(debug, nr, n)
     L = lib()
     stream = stream_ptr(rays.device)
     if q8 is None:
@@ -207,18 +207,166 @@ def _infer_common(points, diffuse, specular, density, adjacency, offsets, rays, 
 _CHECK_ERRORS = False
 
 
-def _debug_struct(debug, nr):
+def _debug_struct(debug, nr, n_points=0):
     """Allocate the optional per-ray diagnostics requested in ``debug`` (a dict
-    that receives the tensors): keys seq_cap, stats, num_intersections."""
+    that receives the tensors): keys seq_cap (visited-cell sequences), visited
+    (per-cell visited / textured flags); stats and num_intersections always."""
     if debug is None:
         return None, None
     dev = torch.device("cuda", torch.cuda.current_device())
     cap = int(debug.get("seq_cap", 0))
-    seq = torch.zeros((nr, cap), dtype=torch.int32, device=dev) if cap else None
-    seq_len = torch.zeros(nr, dtype=torch.int32, device=dev) if cap else None
-    stats = torch.zeros((nr, 4), dtype=torch.int32, device=dev)
-    nint = torch.zeros(nr, dtype=torch.int32, device=dev)
-    debug.update(seq=seq, seq_len=seq_len, stats=stats, num_intersections=nint)
-    d = _lib.VtDebug(seq.data_ptr() if cap else None, cap, seq_len.data_ptr() if cap else None,
-                     stats.data_ptr(), nint.data_ptr())
-    return C.byref(d), (d, seq, seq_len, stats, nint)
+    z = lambda *shape, dt=torch.int32: torch.zeros(shape, dtype=dt, device=dev)
+    seq = z(nr, cap) if cap else None
+    seq_len = z(nr) if cap else None
+    stats = z(nr, 4)
+    nint = z(nr)
+    vis = z(n_points, dt=torch.uint8) if debug.get("visited") else None
+    tex = z(n_points, dt=torch.uint8) if debug.get("visited") else None
+    debug.update(seq=seq, seq_len=seq_len, stats=stats, num_intersections=nint, visited=vis,
+                 textured=tex)
+    a = lambda t: None if t is None else t.data_ptr()
+    d = _lib.VtDebug(a(seq), cap, a(seq_len), a(stats), a(nint), a(vis), a(tex))
+    return C.byref(d), (d, seq, seq_len, stats, nint, vis, tex)
+
+
+# ---------------------------------------------------------------- BVH
+
+def _ws(nbytes: int, device) -> torch.Tensor:
+    return torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=device)
+
+
+class NNBVH:
+    """Nearest-site BVH (replaces the reference's cuBQL-backed NNBVH,
+    vorotracing/cuda/csrc/utils/nn_bvh.cu:43-109).
+
+    build(points) builds it; query(points, queries) returns the int32 index of
+    the nearest site to each query (ties to the lowest index)."""
+
+    def __init__(self):
+        self._nodes = None
+        self.num_points = 0
+
+    def build(self, points):
+        if points.device.type != "cuda":
+            _fail("points must be on CUDA")
+        points = points.detach().contiguous()
+        if points.dtype != torch.float32 or points.dim() != 2 or points.size(1) != 3:
+            _fail("points must be a float32 (N, 3) tensor")
+        n = points.size(0)
+        if n == 0:
+            _fail("points must have at least 1 point")
+        L = lib()
+        nb = int(L.vt_bvh_nodes_bytes(C.c_uint32(n)))
+        wb = int(L.vt_bvh_workspace_bytes(C.c_uint32(n)))
+        nodes = _ws(nb, points.device)
+        ws = _ws(wb, points.device)
+        check(L.vt_bvh_build(ptr(points), C.c_uint32(n), ptr(nodes), C.c_uint64(nb), ptr(ws),
+                             C.c_uint64(wb), stream_ptr(points.device)), "vt_bvh_build")
+        self._nodes = nodes
+        self._ws_keep = ws  # freed on the next build; the stream orders reuse
+        self.num_points = n
+
+    def query(self, points, queries):
+        if self._nodes is None:
+            _fail("BVH must be built before querying")
+        if queries.device.type != "cuda":
+            _fail("queries must be on CUDA")
+        points = points.detach().contiguous()
+        if points.size(0) != self.num_points:
+            _fail("points must be the point set the BVH was built on")
+        q = queries.detach().reshape(-1, 3).contiguous().float()
+        out = torch.empty(q.size(0), dtype=torch.int32, device=q.device)
+        check(lib().vt_bvh_query(ptr(self._nodes), ptr(points), C.c_uint32(self.num_points),
+                                 ptr(q), C.c_uint32(q.size(0)), ptr(out), None,
+                                 stream_ptr(q.device)), "vt_bvh_query")
+        return out
+
+
+def nearest_neighbor_bvh(points, queries):
+    """One-off build + query (nn_bvh.cu:112-117)."""
+    b = NNBVH()
+    b.build(points)
+    return b.query(points, queries)
+
+
+# ---------------------------------------------------------------- layout
+
+def morton_codes(points) -> torch.Tensor:
+    points = points.detach().contiguous()
+    n = points.size(0)
+    codes = torch.empty(n, dtype=torch.int64, device=points.device)
+    ws = _ws(256, points.device)
+    check(lib().vt_morton_codes(ptr(points), C.c_uint32(n), ptr(codes), ptr(ws),
+                                stream_ptr(points.device)), "vt_morton_codes")
+    return codes
+
+
+def morton_perm(points):
+    """(perm, inv_perm) int64: stable argsort of the sites' Morton codes."""
+    points = points.detach().contiguous()
+    n = points.size(0)
+    dev = points.device
+    codes = morton_codes(points)
+    wb = int(lib().vt_morton_workspace_bytes(C.c_uint32(n)))
+    ws = _ws(wb, dev)
+    perm = torch.empty(n, dtype=torch.int32, device=dev)
+    inv = torch.empty(n, dtype=torch.int32, device=dev)
+    check(lib().vt_morton_perm(ptr(codes), C.c_uint32(n), ptr(perm), ptr(inv), ptr(ws),
+                               C.c_uint64(wb), stream_ptr(dev)), "vt_morton_perm")
+    return perm, inv
+
+
+def gather_rows(src: torch.Tensor, perm: torch.Tensor) -> torch.Tensor:
+    src = src.contiguous()
+    out = torch.empty_like(src)
+    n = src.size(0)
+    row = src.numel() // max(n, 1) * src.element_size()
+    check(lib().vt_gather_rows(ptr(src), ptr(out), ptr(perm.contiguous()), C.c_uint32(n),
+                               C.c_uint32(row), stream_ptr(src.device)), "vt_gather_rows")
+    return out
+
+
+def permute_csr(adjacency, offsets, perm, inv, pad: int = 32):
+    n = offsets.numel() - 1
+    dev = offsets.device
+    wb = int(lib().vt_morton_workspace_bytes(C.c_uint32(n)))
+    ws = _ws(wb, dev)
+    new_offs = torch.empty(n + 1, dtype=torch.uint32, device=dev)
+    new_adj = torch.zeros(adjacency.numel(), dtype=torch.uint32, device=dev)
+    check(lib().vt_permute_csr(ptr(offsets.contiguous()), ptr(adjacency.contiguous()),
+                               C.c_uint32(n), ptr(perm), ptr(inv), ptr(new_offs), ptr(new_adj),
+                               ptr(ws), C.c_uint64(wb), stream_ptr(dev)), "vt_permute_csr")
+    return new_adj, new_offs
+
+
+def tile_perm(H: int, W: int, TH: int = 4, TW: int = 8, device=None) -> torch.Tensor:
+    dev = device or torch.device("cuda", torch.cuda.current_device())
+    out = torch.empty(H * W, dtype=torch.int32, device=dev)
+    check(lib().vt_tile_perm(C.c_uint32(H), C.c_uint32(W), C.c_uint32(TH), C.c_uint32(TW),
+                             ptr(out), stream_ptr(dev)), "vt_tile_perm")
+    return out
+
+
+def pad_f16x4(tex: torch.Tensor) -> torch.Tensor:
+    """(N, 3R^2) float32 -> (N, 4R^2) float16 Half4Texel rows."""
+    tex = tex.detach().contiguous().float()
+    n = tex.size(0)
+    out = torch.empty((n, tex.size(1) // 3 * 4), dtype=torch.float16, device=tex.device)
+    check(lib().vt_pad_f16x4(ptr(tex), C.c_uint64(tex.numel() // 3), ptr(out),
+                             stream_ptr(tex.device)), "vt_pad_f16x4")
+    return out
+
+
+def quantize_u8(tex: torch.Tensor):
+    """Global min/max uint8 quantisation -> (q, scale, offset) as Python floats."""
+    tex = tex.detach().contiguous().float()
+    mm = torch.empty(2, dtype=torch.float32, device=tex.device)
+    ws = _ws(256, tex.device)
+    check(lib().vt_minmax_f32(ptr(tex), C.c_uint64(tex.numel()), C.c_int(1), ptr(ws), ptr(mm),
+                              stream_ptr(tex.device)), "vt_minmax_f32")
+    vmin, vmax = (float(v) for v in mm.cpu())
+    scale = (vmax - vmin) / 255.0
+    q = torch.empty(tex.shape, dtype=torch.uint8, device=tex.device)
+    check(lib().vt_quantize_u8(ptr(tex), C.c_uint64(tex.numel()), C.c_float(scale),
+                               C.c_float(vmin), ptr(q), stream_ptr(tex.device)), "vt_quantize_u8")
+    return q, scale, vmin

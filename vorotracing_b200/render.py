@@ -1,0 +1,110 @@
+"""Inference-side scene preparation and rendering (the reference's
+``VoroTracingInfer``, vorotracing/vorotracing.py:439-683), on this package's
+kernels: quantisation / fp16 padding, Morton reordering of cells and CSR,
+BVH start-cell lookup, 4x8 warp-tile ray order, and the inference trace."""
+from __future__ import annotations
+
+from typing import Literal
+
+import torch
+
+from .cuda import _ops
+
+
+class InferScene:
+    """Renderable scene.
+
+    points (N,3) f32; density (N,1) f32 *activated* density; adjacency / offsets
+    uint32 CSR (with tail padding); diffuse / specular (N, 3R^2) f32 logits.
+    """
+
+    def __init__(self, points, density, adjacency, offsets, diffuse, specular,
+                 quantize: Literal["fp16", "q8"] = "fp16", sort_morton: bool = True):
+        dev = points.device
+        self.quantize = quantize
+        self.primal_points = points.detach().contiguous()
+        self.density = density.detach().reshape(-1, 1).contiguous().float()
+        self.point_adjacency = adjacency.contiguous()
+        self.point_adjacency_offsets = offsets.contiguous()
+        if quantize == "q8":
+            self.diffuse_q8, self.diff_scale, self.diff_offset = _ops.quantize_u8(diffuse)
+            self.specular_q8, self.spec_scale, self.spec_offset = _ops.quantize_u8(specular)
+        elif quantize == "fp16":
+            self.diffuse_fp16 = _ops.pad_f16x4(diffuse)
+            self.specular_fp16 = _ops.pad_f16x4(specular)
+        else:
+            raise ValueError(f"Invalid quantization method: {quantize}")
+        if sort_morton:
+            self._reorder_by_morton()
+        self.bvh = _ops.NNBVH()
+        self.bvh.build(self.primal_points)
+        self.adjacent_diff = _ops.prefetch_faces(self.primal_points, self.point_adjacency,
+                                                 self.point_adjacency_offsets)
+        self._tile_cache = {}
+        self.device = dev
+
+    def _reorder_by_morton(self):
+        perm, inv = _ops.morton_perm(self.primal_points)
+        g = lambda t: _ops.gather_rows(t, perm)
+        self.primal_points = g(self.primal_points)
+        self.density = g(self.density)
+        if self.quantize == "q8":
+            self.diffuse_q8, self.specular_q8 = g(self.diffuse_q8), g(self.specular_q8)
+        else:
+            self.diffuse_fp16, self.specular_fp16 = g(self.diffuse_fp16), g(self.specular_fp16)
+        self.point_adjacency, self.point_adjacency_offsets = _ops.permute_csr(
+            self.point_adjacency, self.point_adjacency_offsets, perm, inv)
+        self.perm = perm
+
+    def tile_perm(self, H: int, W: int) -> torch.Tensor:
+        key = (int(H), int(W))
+        if key not in self._tile_cache:
+            self._tile_cache[key] = _ops.tile_perm(H, W, device=self.primal_points.device)
+        return self._tile_cache[key]
+
+    def get_starting_point(self, rays, per_ray: bool = False) -> torch.Tensor:
+        """Start cell per ray.  Default: the first ray's origin cell broadcast to
+        all rays, as the reference does (vorotracing.py:585-604, pinhole views);
+        per_ray=True queries every ray origin (moving or non-pinhole cameras)."""
+        lead = rays.shape[:-1]
+        flat = rays.reshape(-1, rays.shape[-1])
+        if per_ray:
+            idx = self.bvh.query(self.primal_points, flat[:, :3])
+            return idx.view(torch.uint32).reshape(lead)
+        idx = self.bvh.query(self.primal_points, flat[:1, :3])
+        return idx.expand(flat.shape[0]).reshape(lead).contiguous().view(torch.uint32)
+
+    def render(self, rays, start_point=None, weight_threshold=0.001, max_intersections=1024,
+               cell_skip_threshold=0.0, use_warp_perm: bool = True, per_ray_start: bool = False,
+               debug=None):
+        ray_perm = None
+        if use_warp_perm and rays.dim() == 3 and rays.shape[-1] == 6:
+            ray_perm = self.tile_perm(rays.shape[0], rays.shape[1])
+        if start_point is None:
+            start_point = self.get_starting_point(rays, per_ray_start)
+        else:
+            start_point = torch.broadcast_to(start_point, rays.shape[:-1])
+        if self.quantize == "q8":
+            return _ops.trace_vorotracing_infer_q8(
+                self.primal_points, self.diffuse_q8, self.specular_q8, self.density,
+                self.point_adjacency, self.point_adjacency_offsets, rays, start_point,
+                self.adjacent_diff, self.diff_scale, self.diff_offset, self.spec_scale,
+                self.spec_offset, weight_threshold, max_intersections, cell_skip_threshold,
+                ray_perm=ray_perm, debug=debug)
+        return _ops.trace_vorotracing_infer(
+            self.primal_points, self.diffuse_fp16, self.specular_fp16, self.density,
+            self.point_adjacency, self.point_adjacency_offsets, rays, start_point,
+            self.adjacent_diff, ray_perm, weight_threshold, max_intersections,
+            cell_skip_threshold, debug=debug)
+
+    def render_host(self, rays_host: torch.Tensor, out_host: torch.Tensor | None = None,
+                    **kw) -> torch.Tensor:
+        """End-to-end render of host rays (pinned memory recommended): copy in,
+        trace, copy the float16 rgba back.  Returns the host tensor."""
+        rays = rays_host.to(self.primal_points.device, non_blocking=True)
+        rgba = self.render(rays, **kw)
+        if out_host is None:
+            out_host = torch.empty(rgba.shape, dtype=rgba.dtype, pin_memory=True)
+        out_host.copy_(rgba, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        return out_host
