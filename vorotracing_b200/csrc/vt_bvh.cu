@@ -350,3 +350,4 @@ extern "C" vt_status vt_bvh_query(const void *nodes, const float *points, uint32
         nd, ids, points, num_points, queries, num_queries, out, err);
     return vt::check_launch("vt_bvh_query");
 }
+

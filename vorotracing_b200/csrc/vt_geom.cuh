@@ -1,6 +1,9 @@
 // vt_geom.cuh -- vectors, octahedral texture addressing and the packed face
 // record shared by every traversal kernel.  Operation order is part of the
-// parity contract with the CPU oracle (see vt_math.cuh).
+// parity contract with the CPU oracle (see vt_math.cuh): the multiply-adds
+// that nvcc contracts when compiling the reference's expressions are written
+// as explicit fmaf (dot products, face origin, hit point, bilinear blends,
+// octahedral texel coordinates); everything else is one IEEE op per operator.
 #pragma once
 
 #include "vt_math.cuh"
@@ -16,7 +19,12 @@ __device__ __forceinline__ V3 operator+(V3 a, V3 b) { return mk(a.x + b.x, a.y +
 __device__ __forceinline__ V3 operator-(V3 a, V3 b) { return mk(a.x - b.x, a.y - b.y, a.z - b.z); }
 __device__ __forceinline__ V3 operator*(float s, V3 a) { return mk(s * a.x, s * a.y, s * a.z); }
 __device__ __forceinline__ V3 divs(V3 a, float s) { return mk(a.x / s, a.y / s, a.z / s); }
-__device__ __forceinline__ float dot(V3 a, V3 b) { return (a.x * b.x + a.y * b.y) + a.z * b.z; }
+__device__ __forceinline__ float dot(V3 a, V3 b) { return fmaf(a.z, b.z, fmaf(a.y, b.y, a.x * b.x)); }
+// a * s + b per component, contracted
+__device__ __forceinline__ V3 fma3(V3 a, float s, V3 b)
+{
+    return mk(fmaf(a.x, s, b.x), fmaf(a.y, s, b.y), fmaf(a.z, s, b.z));
+}
 __device__ __forceinline__ float norm(V3 a) { return sqrtf(dot(a, a)); }
 __device__ __forceinline__ V3 ld3(const float *__restrict__ p)
 {
@@ -52,8 +60,8 @@ template <int R> __device__ __forceinline__ void oct_encode(V3 dir, float &tu, f
         u = ou;
         v = ov;
     }
-    tu = (u * 0.5f + 0.5f) * (float)R - 0.5f;
-    tv = (v * 0.5f + 0.5f) * (float)R - 0.5f;
+    tu = fmaf(fmaf(u, 0.5f, 0.5f), (float)R, -0.5f);
+    tv = fmaf(fmaf(v, 0.5f, 0.5f), (float)R, -0.5f);
 }
 
 // Octahedral mirror wrap of an out-of-range texel (ray_integrator_octmap.cuh:37-55).
@@ -94,16 +102,19 @@ template <int R> __device__ __forceinline__ Bilin make_bilin(float u, float v)
 
 __device__ __forceinline__ float blend(const Bilin &b, float a00, float a10, float a01, float a11)
 {
-    return ((b.w00 * a00 + b.w10 * a10) + b.w01 * a01) + b.w11 * a11;
+    return fmaf(b.w11, a11, fmaf(b.w01, a01, fmaf(b.w10, a10, b.w00 * a00)));
 }
 
 // Direction from the site to the entry point (ray_integrator_octmap.cuh:258-264).
 __device__ __forceinline__ V3 probe_dir(const Ray &ray, float t0, V3 P)
 {
-    V3 hit = ray.o + t0 * ray.d;
+    V3 hit = fma3(ray.d, t0, ray.o);
     V3 dd = hit - P;
     float len = norm(dd);
-    if (len > 1e-8f) return divs(dd, len);
+    if (len > 1e-8f) {
+        float inv = 1.0f / len;
+        return mk(dd.x * inv, dd.y * inv, dd.z * inv);
+    }
     return ray.d;
 }
 

@@ -61,8 +61,8 @@ template <int R> struct TexQ8 {
             float dv[4], sv[4];
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
-                dv[k] = dscale * (float)a[k][c] + doffset;
-                sv[k] = sscale * (float)b[k][c] + soffset;
+                dv[k] = fmaf(dscale, (float)a[k][c], doffset);
+                sv[k] = fmaf(sscale, (float)b[k][c], soffset);
             }
             r[c] = blend(d, dv[0], dv[1], dv[2], dv[3]) + blend(s, sv[0], sv[1], sv[2], sv[3]);
         }
@@ -101,7 +101,7 @@ template <int R, class Tex> struct InferInteg {
             Bilin d = make_bilin<R>(tu, tv);
             V3 l = tex.logits(cell, d, spec);
             V3 rgb = mk(sigmoid(l.x), sigmoid(l.y), sigmoid(l.z));
-            acc = acc + w * rgb;
+            acc = fma3(rgb, w, acc);
             ntex++;
         }
         T = T * (1.0f - alpha);

@@ -104,13 +104,13 @@ template <class AT, int R> struct FwdInteg {
         float s1 = 1.0f - 1.0f / (1.0f + t1);
         float mid = 0.5f * (s0 + s1);
         float ds = s1 - s0;
-        dist += w * (mid * W - S);
-        self += (w * w) * ds;
+        dist = fmaf(w, fmaf(mid, W, -S), dist);
+        self = fmaf(w * w, ds, self);
         W += w;
-        S += w * mid;
+        S = fmaf(w, mid, S);
         if (t1 > tfar) tfar = t1;
         if (contrib) atomic_add<AT>(contrib + cell, w);
-        acc = acc + w * rgb;
+        acc = fma3(rgb, w, acc);
         float nT = T * (1.0f - alpha);
         while (qi < K && nT < qv) {
             qdepth[qi] = t0 + logf_exact(T / qv) / s;

@@ -55,7 +55,7 @@ __device__ __forceinline__ void test_chunk(const FaceChunk &c, uint32_t j, uint3
         const uint4 f = c.f[k];
         V3 off = mk(h2f((uint16_t)(f.x & 0xffffu)), h2f((uint16_t)(f.x >> 16)),
                     h2f((uint16_t)(f.y & 0xffffu)));
-        V3 fo = P + 0.5f * off;
+        V3 fo = fma3(off, 0.5f, P);
         float dp = dot(off, ray.d);
         float t = dot(fo - ray.o, off) / dp;
         if (j + k < deg && dp > 0.0f && t < x.t1) {

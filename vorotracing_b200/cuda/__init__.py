@@ -4,12 +4,15 @@ layouts and error behaviour, backed by the sm_100a kernels of
 libvorotracing_b200.so."""
 from ._ops import NNBVH, nearest_neighbor_bvh
 from ._wrapper import (
+    ErrorBox,
+    TraceVoroTracing,
     prefetch_octmap_adj,
     trace_octmap_infer,
     trace_octmap_infer_q8,
 )
 
 __all__ = [
+    "TraceVoroTracing",
     "trace_octmap_infer",
     "trace_octmap_infer_q8",
     "prefetch_octmap_adj",

@@ -370,3 +370,191 @@ def quantize_u8(tex: torch.Tensor):
     check(lib().vt_quantize_u8(ptr(tex), C.c_uint64(tex.numel()), C.c_float(scale),
                                C.c_float(vmin), ptr(q), stream_ptr(tex.device)), "vt_quantize_u8")
     return q, scale, vmin
+
+
+# ---------------------------------------------------------------- training
+
+def _attr_half(diffuse) -> int:
+    if diffuse.dtype == torch.float32:
+        return 0
+    if diffuse.dtype == torch.float16:
+        return 1
+    _fail("Unsupported color dtype. Only float32 and float16 are supported.")
+
+
+def _train_checks(points, diffuse, specular, density, adjacency, offsets, rays, start_point):
+    validate_scene_data(points, diffuse, adjacency, offsets)
+    n = points.size(0)
+    if diffuse.dtype != specular.dtype:
+        _fail("diffuse and specular must have the same dtype")
+    if not (diffuse.size(0) == specular.size(0) == density.size(0) == n):
+        _fail("diffuse, specular, density must each have num_points rows")
+    if density.dtype != torch.float32:
+        _fail("density must have float32 dtype")
+    if rays.size(-1) != 6:
+        _fail("rays must have 6 as the last dimension")
+    if rays.dtype != torch.float32:
+        _fail("rays must have float32 dtype")
+    if rays.device.type != "cuda":
+        _fail("rays must be on CUDA device")
+    nr = rays.numel() // 6
+    if start_point.numel() != nr:
+        _fail("start_point must have the same batch size as rays")
+    if start_point.dtype != torch.uint32:
+        _fail("start_point must have uint32 dtype")
+    if start_point.device.type != "cuda":
+        _fail("start_point must be on CUDA device")
+    return nr
+
+
+def trace_vorotracing_fwd(points, diffuse, specular, density, adjacency, offsets, rays,
+                          start_point, depth_quantiles, weight_threshold: float,
+                          max_intersections: int, return_contribution: bool, faces=None,
+                          debug: dict | None = None):
+    """Training forward (tracing_octmap.cu:355-546).  Returns the reference's
+    9-tuple (rgba, depth, depth_indices, contribution, num_intersections,
+    distortion, W_total, S_total, t_far); depth / depth_indices /
+    contribution are None when not requested."""
+    points, diffuse, specular = points.contiguous(), diffuse.contiguous(), specular.contiguous()
+    density, adjacency, offsets = density.contiguous(), adjacency.contiguous(), offsets.contiguous()
+    rays, start_point = _aligned(rays, 8), start_point.contiguous()
+    nr = _train_checks(points, diffuse, specular, density, adjacency, offsets, rays, start_point)
+    half = _attr_half(diffuse)
+    res = _res_from(diffuse, 3)
+    if _res_from(specular, 3) != res:
+        _fail("diffuse and specular octahedral resolutions must match")
+    dev = rays.device
+    lead = tuple(rays.shape[:-1])
+    K = 0
+    dq = None
+    if depth_quantiles is not None:
+        dq = depth_quantiles.contiguous()
+        K = dq.size(-1)
+        if dq.dtype != torch.float32:
+            _fail("depth_quantiles must have float32 dtype")
+        if dq.device.type != "cuda":
+            _fail("depth_quantiles must be on CUDA device")
+        if K == 0 or dq.numel() // K != nr:
+            _fail("depth_quantiles must have the same batch size as rays")
+    rgba = torch.empty(lead + (4,), dtype=diffuse.dtype, device=dev)
+    n_int = torch.empty(lead + (1,), dtype=torch.uint32, device=dev)
+    contrib = (torch.zeros((points.size(0), 1), dtype=diffuse.dtype, device=dev)
+               if return_contribution else None)
+    depth = depth_idx = None
+    if dq is not None:
+        depth = torch.zeros(lead + (K,), dtype=torch.float32, device=dev)
+        depth_idx = torch.zeros(lead + (K,), dtype=torch.uint32, device=dev)
+    f32 = lambda: torch.empty(lead + (1,), dtype=torch.float32, device=dev)
+    dist, W, S, tfar = f32(), f32(), f32(), f32()
+    if faces is None:
+        faces = prefetch_faces(points, adjacency, offsets)
+    scene = make_scene(points, density, offsets, faces)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    dbg, keep = _debug_struct(debug, nr, points.size(0))
+    check(lib().vt_trace_fwd(C.byref(scene), C.c_int(half), ptr(diffuse), ptr(specular),
+                             C.c_int(res), ptr(rays), C.c_uint32(nr), ptr(start_point),
+                             C.c_uint32(K), ptr(dq), C.c_float(weight_threshold),
+                             C.c_uint32(max_intersections), ptr(rgba), ptr(depth), ptr(depth_idx),
+                             ptr(n_int), ptr(contrib), ptr(dist), ptr(W), ptr(S), ptr(tfar), dbg,
+                             ptr(err), stream_ptr(dev)), "vt_trace_fwd")
+    if debug is not None or _CHECK_ERRORS:
+        _check_err(err)
+    del keep
+    return rgba, depth, depth_idx, contrib, n_int, dist, W, S, tfar
+
+
+def trace_vorotracing_bwd(points, diffuse, specular, density, adjacency, offsets, rays,
+                          start_point, rgb_out, rgb_grad_in, depth_quantiles, depth_indices,
+                          depth_grad, ray_error, contribution_alpha_grad: float, distortion,
+                          distortion_grad, W_total, S_total, t_far, weight_threshold: float,
+                          max_intersections: int, faces=None):
+    """Training backward (tracing_octmap.cu:860-1103).  Returns the reference's
+    6-tuple (points_grad, diffuse_grad, specular_grad, density_grad, ray_grad,
+    point_error); ray_grad is allocated and never written, as in the
+    reference; point_error is None unless ray_error is given."""
+    points, diffuse, specular = points.contiguous(), diffuse.contiguous(), specular.contiguous()
+    density, adjacency, offsets = density.contiguous(), adjacency.contiguous(), offsets.contiguous()
+    rays, start_point = _aligned(rays, 8), start_point.contiguous()
+    nr = _train_checks(points, diffuse, specular, density, adjacency, offsets, rays, start_point)
+    half = _attr_half(diffuse)
+    res = _res_from(diffuse, 3)
+    dev = rays.device
+    g = rgb_grad_in.contiguous()
+    if g.size(-1) != 4:
+        _fail("rgb_grad_in must have 4 as the last dimension")
+    if g.dtype != diffuse.dtype:
+        _fail("rgb_grad_in must have the same dtype as diffuse/specular")
+    if g.device.type != "cuda":
+        _fail("rgb_grad_in must be on CUDA device")
+    if g.numel() // 4 != nr:
+        _fail("rgb_grad_in must have the same batch size as rays")
+    rgb_out = rgb_out.contiguous()
+    K = 0
+    dq = di = dg = None
+    if depth_quantiles is not None:
+        dq = depth_quantiles.contiguous()
+        K = dq.size(-1)
+        if dq.dtype != torch.float32:
+            _fail("depth_quantiles must have float32 dtype")
+        if dq.numel() != nr * K:
+            _fail("depth_quantiles must have the same batch size as rays")
+        if depth_grad is None:
+            _fail("depth_grad must be provided if depth_quantiles is provided")
+        di = depth_indices.contiguous()
+        if di.dtype != torch.uint32:
+            _fail("depth_indices must have uint32 dtype")
+        if di.numel() != nr * K:
+            _fail("depth_indices must have the same batch size as rays")
+        dg = depth_grad.contiguous()
+        if dg.size(-1) != K:
+            _fail("depth_grad must have the same number of depth quantiles as depth_quantiles")
+        if dg.dtype != torch.float32:
+            _fail("depth_grad must have float32 dtype")
+        if dg.numel() != nr * K:
+            _fail("depth_grad must have the same batch size as rays")
+    perr = re = None
+    n = points.size(0)
+    if ray_error is not None:
+        re = ray_error.contiguous()
+        if re.dtype != diffuse.dtype:
+            _fail("ray_error must have the same dtype as diffuse/specular")
+        if re.numel() != nr:
+            _fail("ray_error must have the same batch size as rays")
+        perr = torch.zeros((n, 1), dtype=diffuse.dtype, device=dev)
+    ts = {}
+    for name, t in (("W_total", W_total), ("S_total", S_total), ("t_far", t_far),
+                    ("distortion", distortion)):
+        t = t.contiguous()
+        if t.dtype != torch.float32:
+            _fail(f"{name} must have float32 dtype")
+        if t.numel() != nr:
+            _fail(f"{name} must have the same batch size as rays")
+        ts[name] = t
+    dgr = None
+    if distortion_grad is not None:
+        dgr = distortion_grad.contiguous()
+        if dgr.dtype != torch.float32:
+            _fail("distortion_grad must have float32 dtype")
+        if dgr.numel() != nr:
+            _fail("distortion_grad must have the same batch size as rays")
+    diffuse_grad = torch.zeros_like(diffuse)
+    specular_grad = torch.zeros_like(specular)
+    density_grad = torch.zeros_like(density, dtype=torch.float32)
+    points_grad = torch.zeros((n, 3), dtype=torch.float32, device=dev)
+    ray_grad = torch.empty_like(rays)
+    if faces is None:
+        faces = prefetch_faces(points, adjacency, offsets)
+    scene = make_scene(points, density, offsets, faces)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    check(lib().vt_trace_bwd(C.byref(scene), C.c_int(half), ptr(diffuse), ptr(specular),
+                             C.c_int(res), ptr(rays), C.c_uint32(nr), ptr(start_point),
+                             C.c_uint32(K), ptr(dq), ptr(di), ptr(rgb_out), ptr(g), ptr(dg),
+                             ptr(re), C.c_float(contribution_alpha_grad),
+                             ptr(ts["distortion"]), ptr(dgr), ptr(ts["W_total"]),
+                             ptr(ts["S_total"]), C.c_float(weight_threshold),
+                             C.c_uint32(max_intersections), ptr(points_grad), ptr(diffuse_grad),
+                             ptr(specular_grad), ptr(density_grad), ptr(perr), ptr(err),
+                             stream_ptr(dev)), "vt_trace_bwd")
+    if _CHECK_ERRORS:
+        _check_err(err)
+    return points_grad, diffuse_grad, specular_grad, density_grad, ray_grad, perr
