@@ -10,7 +10,7 @@
 // strictly farther than the best site so far.
 //
 // Exact contract (matches the CPU oracle's brute force): the answer minimises
-// d2 = (dx*dx + dy*dy) + dz*dz in binary32, ties to the lowest site index.
+// d2 = fma(dz,dz, fma(dy,dy, dx*dx)) in binary32, ties to the lowest site index.
 // The box bound is computed with the same rounded operations, and RN is
 // monotone, so a box bound never exceeds the d2 of any site inside it.
 //
@@ -178,7 +178,9 @@ __device__ __forceinline__ float box_d2(const Node &b, V3 q)
     float dx = fmaxf(fmaxf(b.lo[0] - q.x, 0.0f), q.x - b.hi[0]);
     float dy = fmaxf(fmaxf(b.lo[1] - q.y, 0.0f), q.y - b.hi[1]);
     float dz = fmaxf(fmaxf(b.lo[2] - q.z, 0.0f), q.z - b.hi[2]);
-    return (dx * dx + dy * dy) + dz * dz;
+    // same contracted form as the site distance dot(d, d), so the bound stays
+    // below the distance of every site in the box (RN and fma are monotone)
+    return dot(mk(dx, dy, dz), mk(dx, dy, dz));
 }
 
 __device__ __forceinline__ void visit_leaf(const float *__restrict__ p, uint32_t id, V3 q,
