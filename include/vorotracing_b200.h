@@ -152,6 +152,18 @@ VT_API uint64_t vt_bvh_workspace_bytes(uint32_t num_points);
 VT_API vt_status vt_bvh_build(const float *points, uint32_t num_points, void *nodes,
                               uint64_t nodes_bytes, void *workspace, uint64_t workspace_bytes,
                               vt_stream stream);
+/* Same build as vt_bvh_build, for callers that cannot allocate device
+ * memory (an application that lends this library only its input and output
+ * buffers, or a binding without a CUDA allocator): its scratch is a fixed
+ * 32 MiB array inside the library, held on every GPU that loads it, so it
+ * takes no workspace argument and accepts at most VT_BVH_NOALLOC_MAX_POINTS
+ * sites (more: VT_ERR_INVALID).  The first call on a device looks up the
+ * array's device address; make it before any stream capture.  Calls share
+ * the array: calls that overlap on the GPU race, so serialise them.
+ * No counterpart in the reference. */
+#define VT_BVH_NOALLOC_MAX_POINTS 1048576u
+VT_API vt_status vt_bvh_build_noalloc(const float *points, uint32_t num_points, void *nodes,
+                                      uint64_t nodes_bytes, vt_stream stream);
 /* out[q] = index of the site nearest to queries[q] (squared distance in
  * binary32, ties to the lowest index), int32. */
 VT_API vt_status vt_bvh_query(const void *nodes, const float *points, uint32_t num_points,

@@ -353,3 +353,69 @@ extern "C" vt_status vt_bvh_query(const void *nodes, const float *points, uint32
     return vt::check_launch("vt_bvh_query");
 }
 
+// ---------------------------------------------------------------------------
+// Allocation-free BVH build.
+//
+// Some callers cannot allocate device memory themselves: a host application
+// that hands this library only its input and output buffers and keeps every
+// other byte of device memory under its own budget, or a binding whose
+// language runtime has no CUDA allocator to offer.  vt_bvh_build_noalloc
+// gives them the start-cell BVH build with its scratch in a fixed array that
+// lives in this file (kNoAllocScratchBytes on every GPU that loads the
+// library, held until the process exits).  Sites are limited to
+// VT_BVH_NOALLOC_MAX_POINTS.
+//
+// Host code cannot pass the array's name to a kernel: on the host that name
+// is only a stand-in symbol, not a device address.  The first call on each
+// device resolves the device address with cudaGetSymbolAddress (with that
+// device current) and caches it; make that first call before any stream
+// capture.  All calls share the one array, so calls whose work overlaps on
+// the GPU (different streams, or different host threads on one device) race
+// on it; serialise them.  The array keeps the previous call's contents: every
+// field the build reads (bounding box, sort buffers, parent links, the
+// per-node arrival counters) is rewritten by the build before it is read.
+// ---------------------------------------------------------------------------
+#include <mutex>
+
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(32) << 20;
+static __device__ __align__(256) unsigned char g_bvh_noalloc_scratch[kNoAllocScratchBytes];
+
+std::mutex g_noalloc_mu;
+void *g_noalloc_ptr[256] = {};
+
+}  // namespace
+
+extern "C" vt_status vt_bvh_build_noalloc(const float *points, uint32_t num_points, void *nodes,
+                                          uint64_t nodes_bytes, vt_stream stream)
+{
+    VT_REQUIRE(num_points <= VT_BVH_NOALLOC_MAX_POINTS,
+               "vt_bvh_build_noalloc: %u sites exceed the limit of %u for the fixed scratch "
+               "array; use vt_bvh_build with a caller-provided workspace",
+               num_points, (unsigned)VT_BVH_NOALLOC_MAX_POINTS);
+    const uint64_t need = vt_bvh_workspace_bytes(num_points);
+    VT_REQUIRE(need <= kNoAllocScratchBytes,
+               "vt_bvh_build_noalloc: %llu scratch bytes needed, %llu available",
+               (unsigned long long)need, (unsigned long long)kNoAllocScratchBytes);
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess)
+        return vt::set_error(VT_ERR_CUDA, "vt_bvh_build_noalloc: %s", cudaGetErrorString(e));
+    VT_REQUIRE(dev >= 0 && dev < 256, "vt_bvh_build_noalloc: device index %d out of range", dev);
+    void *scratch = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(g_noalloc_mu);
+        if (!g_noalloc_ptr[dev]) {
+            void *p = nullptr;
+            e = cudaGetSymbolAddress(&p, g_bvh_noalloc_scratch);
+            if (e != cudaSuccess)
+                return vt::set_error(VT_ERR_CUDA, "vt_bvh_build_noalloc: cudaGetSymbolAddress: %s",
+                                     cudaGetErrorString(e));
+            g_noalloc_ptr[dev] = p;
+        }
+        scratch = g_noalloc_ptr[dev];
+    }
+    return vt_bvh_build(points, num_points, nodes, nodes_bytes, scratch, kNoAllocScratchBytes,
+                        stream);
+}
