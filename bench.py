@@ -99,16 +99,17 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def load_scene(rank: int, ws: int):
+def load_scene(rank: int, ws: int, name: str = "C2"):
+    """Scene arrays of a configuration; rank 0 builds the Delaunay cache first."""
     from vorotracing_b200 import scene as sc
 
     if ws > 1:
         import torch.distributed as dist
 
         if rank == 0:
-            sc.config_scene("C2")
+            sc.config_scene(name)
         dist.barrier()
-    return sc.config_scene("C2")
+    return sc.config_scene(name)
 
 
 def compulsory_bytes(scene, rays, start, dbg_ops):
@@ -209,11 +210,17 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--config", default="C2", choices=["C2", "C3", "C4", "C5"],
+                    help="C2 (default, the headline) or another benchmark configuration")
     ap.add_argument("--profile", action="store_true",
                     help="a few untimed renders only (for ncu captures)")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
+    if args.config != "C2":
+        import bench_configs
+
+        return bench_configs.run(args)
 
     import torch
 

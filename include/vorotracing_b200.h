@@ -142,6 +142,28 @@ VT_API vt_status vt_trace_bwd(const vt_scene *scene, int attr_half, const void *
                               void *specular_grad, float *density_grad, void *point_error,
                               uint32_t *err, vt_stream stream);
 
+/* ---- cameras (ray generation for the benchmark views) ---- */
+
+#define VT_CAMERA_PINHOLE 0   /* generate_camera_rays, vorotracing/utils/__init__.py:85-130 */
+#define VT_CAMERA_FISHEYE 1   /* equidistant r = f * theta; no counterpart in the reference */
+#define VT_CAMERA_ROLLING 2   /* pinhole, centre moving during the row readout; no counterpart */
+#define VT_CAMERA_THIN_LENS 3 /* depth of field, spp lens samples per pixel; no counterpart */
+
+typedef struct {
+    float K[4];         /* fx, fy, cx, cy (pixels) */
+    float c2w[12];      /* camera-to-world 3x4 row-major, OpenCV axes (x right, y down, z fwd) */
+    uint32_t width, height, spp;
+    int32_t model;      /* VT_CAMERA_* */
+    float rs_duration;  /* rolling shutter: readout time of the whole frame (s) */
+    float velocity[3];  /* rolling shutter: camera centre velocity (world units / s) */
+    float lens_radius;  /* thin lens */
+    float focus_distance;
+    uint32_t seed;      /* thin lens sample jitter */
+} vt_camera;
+
+/* rays (height, width, spp, 6) f32: origin, unit direction. */
+VT_API vt_status vt_raygen(const vt_camera *cam, float *rays, vt_stream stream);
+
 /* ---- ray-origin cell lookup (nearest site) ---- */
 
 /* Size of the BVH blob (internal nodes + leaf ids) for num_points sites. */

@@ -174,3 +174,24 @@ def test_fwd_validation_messages(c1_scene, c1_rays):
     with pytest.raises(RuntimeError, match="same dtype"):
         _ops.trace_vorotracing_fwd(g["points"], g["diffuse"], g["specular"].half(), g["density"],
                                    g["adj"], g["offs"], rays, _dev(start), None, 0.01, 1024, False)
+
+
+def test_bwd_into_flat_bucket(c1_scene, c1_rays):
+    """The backward writes into caller-provided views of one flat all-reduce
+    bucket with the same result as into its own tensors."""
+    from vorotracing_b200.cuda import _ops
+    from vorotracing_b200.shard import GradBucket
+
+    s = c1_scene
+    rays = c1_rays[::4, ::4].reshape(-1, 6)
+    S, start, g = _setup(s, rays, False)
+    args = (g["points"], g["diffuse"], g["specular"], g["density"], g["adj"], g["offs"],
+            _dev(rays), _dev(start))
+    f = _ops.trace_vorotracing_fwd(*args, None, 0.01, 1024, False)
+    gr = torch.randn_like(f[0])
+    common = (f[0], gr, None, None, None, None, 0.0, f[5], None, f[6], f[7], f[8], 0.01, 1024)
+    ref = _ops.trace_vorotracing_bwd(*args, *common)
+    b = GradBucket(g["points"].size(0), g["diffuse"].size(1), "cuda")
+    _ops.trace_vorotracing_bwd(*args, *common, grads=b.views())
+    for got, want in zip(b.views(), (ref[0], ref[1], ref[2], ref[3])):
+        torch.testing.assert_close(got.reshape(want.shape), want, rtol=1e-5, atol=1e-6)

@@ -467,9 +467,10 @@ def trace_vorotracing_bwd(points, diffuse, specular, density, adjacency, offsets
                           start_point, rgb_out, rgb_grad_in, depth_quantiles, depth_indices,
                           depth_grad, ray_error, contribution_alpha_grad: float, distortion,
                           distortion_grad, W_total, S_total, t_far, weight_threshold: float,
-                          max_intersections: int, faces=None):
-    """Training backward (tracing_octmap.cu:860-1103).  Returns the reference's
-    6-tuple (points_grad, diffuse_grad, specular_grad, density_grad, ray_grad,
+                          max_intersections: int, faces=None, grads=None):
+    """Training backward (tracing_octmap.cu:860-1103).  Gradients go to new
+    zeroed tensors, or accumulate into ``grads`` = (points, diffuse, specular,
+    density) when given.  Returns the reference's 6-tuple (points_grad, diffuse_grad, specular_grad, density_grad, ray_grad,
     point_error); ray_grad is allocated and never written, as in the
     reference; point_error is None unless ray_error is given."""
     points, diffuse, specular = points.contiguous(), diffuse.contiguous(), specular.contiguous()
@@ -537,10 +538,22 @@ def trace_vorotracing_bwd(points, diffuse, specular, density, adjacency, offsets
             _fail("distortion_grad must have float32 dtype")
         if dgr.numel() != nr:
             _fail("distortion_grad must have the same batch size as rays")
-    diffuse_grad = torch.zeros_like(diffuse)
-    specular_grad = torch.zeros_like(specular)
-    density_grad = torch.zeros_like(density, dtype=torch.float32)
-    points_grad = torch.zeros((n, 3), dtype=torch.float32, device=dev)
+    if grads is None:
+        diffuse_grad = torch.zeros_like(diffuse)
+        specular_grad = torch.zeros_like(specular)
+        density_grad = torch.zeros_like(density, dtype=torch.float32)
+        points_grad = torch.zeros((n, 3), dtype=torch.float32, device=dev)
+    else:
+        # caller-provided, zero-initialised (e.g. views of a flat all-reduce bucket)
+        points_grad, diffuse_grad, specular_grad, density_grad = grads
+        if (points_grad.shape != (n, 3) or points_grad.dtype != torch.float32
+                or diffuse_grad.shape != diffuse.shape or diffuse_grad.dtype != diffuse.dtype
+                or specular_grad.shape != specular.shape
+                or specular_grad.dtype != specular.dtype or density_grad.numel() != n
+                or density_grad.dtype != torch.float32
+                or not all(t.is_contiguous() for t in grads)):
+            _fail("grads must be contiguous (points (N,3) f32, diffuse / specular like the "
+                  "attributes, density (N,) f32)")
     ray_grad = torch.empty_like(rays)
     if faces is None:
         faces = prefetch_faces(points, adjacency, offsets)
