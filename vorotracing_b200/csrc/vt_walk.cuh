@@ -13,7 +13,11 @@
 // its site and its density, and only then integrates the current segment
 // (texture loads included).  One dependent memory round trip per cell
 // remains, and the texture fetch overlaps it.  Face rows are read in chunks
-// of four 128-bit loads with the following chunk prefetched (double buffer).
+// of kChunk 128-bit loads, two chunk buffers used in turn (the next chunk is
+// loaded while the current one is tested, with no register copies), and the
+// scan keeps only the winning distance and face index; the winning record is
+// read again (an L1 hit) once the row is done.  Measured on the C2 view:
+// index tracking + alternating buffers 6.47 -> 5.47 ms, kChunk 4 -> 2 5.36 ms.
 #pragma once
 
 #include "vt_geom.cuh"
@@ -29,15 +33,20 @@ struct WalkDebug {
     uint8_t *textured;  // (cells) 1 if any ray reads the cell's texels
 };
 
+#ifndef VT_CHUNK
+#define VT_CHUNK 2
+#endif
+constexpr uint32_t kChunk = VT_CHUNK;
+
 struct FaceChunk {
-    uint4 f[4];
+    uint4 f[kChunk];
 };
 
 __device__ __forceinline__ void load_chunk(FaceChunk &c, const uint4 *__restrict__ row, uint32_t j,
                                            uint32_t deg)
 {
 #pragma unroll
-    for (int k = 0; k < 4; ++k)
+    for (int k = 0; k < (int)kChunk; ++k)
         if (j + k < deg) c.f[k] = __ldg(row + j + k);
 }
 
@@ -47,23 +56,21 @@ struct ExitFace {
     bool found;
 };
 
-__device__ __forceinline__ void test_chunk(const FaceChunk &c, uint32_t j, uint32_t deg, V3 P,
-                                           const Ray &ray, ExitFace &x)
+// Winner tracked by index only; the record is re-read (L1) after the row.
+__device__ __forceinline__ void test_chunk_idx(const FaceChunk &c, uint32_t j, uint32_t deg, V3 P,
+                                               const Ray &ray, float &t1, uint32_t &jbest)
 {
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
+    for (int k = 0; k < (int)kChunk; ++k) {
         const uint4 f = c.f[k];
         V3 off = mk(h2f((uint16_t)(f.x & 0xffffu)), h2f((uint16_t)(f.x >> 16)),
                     h2f((uint16_t)(f.y & 0xffffu)));
         V3 fo = fma3(off, 0.5f, P);
         float dp = dot(off, ray.d);
         float t = dot(fo - ray.o, off) / dp;
-        if (j + k < deg && dp > 0.0f && t < x.t1) {
-            x.t1 = t;
-            x.nb = f.z;
-            x.nbeg = f.w;
-            x.ndeg = f.y >> 16;
-            x.found = true;
+        if (j + k < deg && dp > 0.0f && t < t1) {
+            t1 = t;
+            jbest = j + k;
         }
     }
 }
@@ -104,12 +111,25 @@ __device__ __forceinline__ uint32_t walk(const Ray &ray, const uint4 *__restrict
         x.found = false;
         x.nb = x.nbeg = x.ndeg = 0;
         const uint4 *row = faces + begin;
-        for (uint32_t j = 0; j < deg; j += 4) {
-            FaceChunk nxt;
-            load_chunk(nxt, row, j + 4, deg);
-            test_chunk(c, j, deg, P, ray, x);
-            c = nxt;
+        {
+            FaceChunk b;
+            uint32_t jbest = 0xffffffffu;
+            for (uint32_t j = 0; j < deg; j += 2 * kChunk) {
+                load_chunk(b, row, j + kChunk, deg);
+                test_chunk_idx(c, j, deg, P, ray, x.t1, jbest);
+                if (j + kChunk >= deg) break;
+                load_chunk(c, row, j + 2 * kChunk, deg);
+                test_chunk_idx(b, j + kChunk, deg, P, ray, x.t1, jbest);
+            }
+            if (jbest != 0xffffffffu) {
+                const uint4 f = __ldg(row + jbest);
+                x.nb = f.z;
+                x.nbeg = f.w;
+                x.ndeg = f.y >> 16;
+                x.found = true;
+            }
         }
+
         if (!x.found) break;
         // Issue the next cell's loads before integrating this one.
         V3 Q = ld3(points + (size_t)x.nb * 3);
