@@ -140,7 +140,14 @@ VT_API vt_status vt_trace_bwd(const vt_scene *scene, int attr_half, const void *
                               const float *W_total, const float *S_total, float weight_threshold,
                               uint32_t max_intersections, float *points_grad, void *diffuse_grad,
                               void *specular_grad, float *density_grad, void *point_error,
-                              uint32_t *err, vt_stream stream);
+                              void *workspace, uint64_t workspace_bytes, uint32_t *err,
+                              vt_stream stream);
+/* Optional scratch of vt_trace_bwd (256-byte aligned): with it the texel and
+ * site gradients accumulate in padded fp32 rows with one vector atomic per
+ * texel (instead of three scalar atomics) and are added to the outputs at the
+ * end; fp16 gradients are then summed in fp32 and rounded once.  Pass null
+ * to accumulate straight into the outputs. */
+VT_API uint64_t vt_trace_bwd_workspace_bytes(uint32_t num_points, int res);
 
 /* ---- cameras (ray generation for the benchmark views) ---- */
 

@@ -195,3 +195,24 @@ def test_bwd_into_flat_bucket(c1_scene, c1_rays):
     _ops.trace_vorotracing_bwd(*args, *common, grads=b.views())
     for got, want in zip(b.views(), (ref[0], ref[1], ref[2], ref[3])):
         torch.testing.assert_close(got.reshape(want.shape), want, rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.parametrize("half", [False, True])
+def test_bwd_vector_atomics_match_scalar(c1_scene, c1_rays, half):
+    """Padded-scratch vector atomics and scalar atomics into the outputs give
+    the same gradients (up to summation order; fp16 is summed in fp32 first)."""
+    from vorotracing_b200.cuda import _ops
+
+    s = c1_scene
+    rays = c1_rays[::2, ::2].reshape(-1, 6)
+    S, start, g = _setup(s, rays, half)
+    args = (g["points"], g["diffuse"], g["specular"], g["density"], g["adj"], g["offs"],
+            _dev(rays), _dev(start))
+    f = _ops.trace_vorotracing_fwd(*args, None, 0.01, 1024, False)
+    gr = torch.randn_like(f[0].float()).to(f[0].dtype)
+    common = (f[0], gr, None, None, None, None, 0.0, f[5], None, f[6], f[7], f[8], 0.01, 1024)
+    a = _ops.trace_vorotracing_bwd(*args, *common, vector_atomics=True)
+    b = _ops.trace_vorotracing_bwd(*args, *common, vector_atomics=False)
+    for x, y, name in zip(a[:4], b[:4], ("points", "diffuse", "specular", "density")):
+        tol, frac = (1e-1, 2e-2) if half and name in ("diffuse", "specular") else (1e-3, 1e-4)
+        _close(x.float().cpu().numpy(), y.float().cpu().numpy(), tol, frac, name)

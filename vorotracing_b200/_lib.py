@@ -41,7 +41,8 @@ def lib():
         L.vt_face_rows.argtypes = [C.c_uint64]
         for name in exported_symbols():
             getattr(L, name)  # every declared entry point must be exported
-        for name in ("vt_bvh_nodes_bytes", "vt_bvh_workspace_bytes", "vt_morton_workspace_bytes"):
+        for name in ("vt_bvh_nodes_bytes", "vt_bvh_workspace_bytes", "vt_morton_workspace_bytes",
+                     "vt_trace_bwd_workspace_bytes"):
             if hasattr(L, name):
                 getattr(L, name).restype = C.c_uint64
         _lib = L

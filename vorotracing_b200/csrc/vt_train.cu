@@ -84,6 +84,7 @@ template <class AT> struct BwdIn {
     AT *diffuse_grad, *specular_grad;
     float *density_grad;
     AT *point_error;
+    float4 *sdiff, *sspec, *spts;  // padded scratch or null
 };
 
 template <class AT, int R>
@@ -141,6 +142,9 @@ __global__ void __launch_bounds__(kTrainBlock)
     I.dspec = b.specular_grad;
     I.dden = b.density_grad;
     I.perr = b.point_error;
+    I.sdiff = b.sdiff;
+    I.sspec = b.sspec;
+    I.spts = b.spts;
     I.prev_geom = I.prev_grad = I.cur_grad = I.next_grad = mk(0.f, 0.f, 0.f);
     I.prev_idx = 0xffffffffu;
     float tu, tv;
@@ -150,6 +154,21 @@ __global__ void __launch_bounds__(kTrainBlock)
     walk<BwdInteg<AT, R>, false>(ray, a.faces, a.offs, a.points, a.density, start, a.max_steps, I,
                                  r, none);
 }
+
+// out[t*3 + c] += scratch[t].c for every texel (or site) t.
+template <class AT>
+__global__ void compact4_kernel(const float4 *__restrict__ scratch, uint64_t n, AT *__restrict__ out)
+{
+    uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= n) return;
+    float4 v = scratch[t];
+    AT *o = out + t * 3;
+    o[0] = fromf<AT>(tof<AT>(o[0]) + v.x);
+    o[1] = fromf<AT>(tof<AT>(o[1]) + v.y);
+    o[2] = fromf<AT>(tof<AT>(o[2]) + v.z);
+}
+
+inline size_t a256(size_t x) { return (x + 255) & ~(size_t)255; }
 
 vt_status fill_common(TrainCommon &a, const vt_scene *scene, const float *rays, uint32_t nr,
                       const uint32_t *start, uint32_t K, const float *dq, float wt,
@@ -181,11 +200,28 @@ vt_status launch_fwd(const TrainCommon &a, const void *dif, const void *spe, con
 }
 
 template <class AT, int R>
-vt_status launch_bwd(const TrainCommon &a, const void *dif, const void *spe, const BwdIn<AT> &b,
-                     cudaStream_t s)
+vt_status launch_bwd(const TrainCommon &a, const void *dif, const void *spe, BwdIn<AT> b,
+                     void *ws, cudaStream_t s)
 {
     TexPlain<AT, R> t{(const AT *)dif, (const AT *)spe};
+    const uint64_t ntex = (uint64_t)a.n_points * R * R;
+    if (ws) {
+        char *w = (char *)ws;
+        b.sdiff = (float4 *)w;
+        b.sspec = (float4 *)(w + a256(ntex * 16));
+        b.spts = (float4 *)(w + 2 * a256(ntex * 16));
+        cudaError_t e = cudaMemsetAsync(ws, 0, 2 * a256(ntex * 16) + a256((size_t)a.n_points * 16), s);
+        if (e != cudaSuccess) return set_error(VT_ERR_CUDA, "vt_trace_bwd memset: %s", cudaGetErrorString(e));
+    } else {
+        b.sdiff = b.sspec = b.spts = nullptr;
+    }
     bwd_kernel<AT, R><<<grid_for(a.num_rays, kTrainBlock), kTrainBlock, 0, s>>>(a, t, b);
+    if (ws) {
+        compact4_kernel<AT><<<grid_for(ntex, 256), 256, 0, s>>>(b.sdiff, ntex, b.diffuse_grad);
+        compact4_kernel<AT><<<grid_for(ntex, 256), 256, 0, s>>>(b.sspec, ntex, b.specular_grad);
+        compact4_kernel<float><<<grid_for(a.n_points, 256), 256, 0, s>>>(b.spts, a.n_points,
+                                                                          b.points_grad);
+    }
     return check_launch("bwd_kernel");
 }
 
@@ -230,6 +266,12 @@ extern "C" vt_status vt_trace_fwd(const vt_scene *scene, int attr_half, const vo
     return vt::set_error(VT_ERR_INVALID, "vt_trace_fwd: res must be 4 or 8, got %d", res);
 }
 
+extern "C" uint64_t vt_trace_bwd_workspace_bytes(uint32_t num_points, int res)
+{
+    const uint64_t ntex = (uint64_t)num_points * res * res;
+    return 2 * vt::a256(ntex * 16) + vt::a256((size_t)num_points * 16);
+}
+
 extern "C" vt_status vt_trace_bwd(const vt_scene *scene, int attr_half, const void *diffuse,
                                   const void *specular, int res, const float *rays,
                                   uint32_t num_rays, const uint32_t *start,
@@ -241,12 +283,17 @@ extern "C" vt_status vt_trace_bwd(const vt_scene *scene, int attr_half, const vo
                                   const float *W_total, const float *S_total,
                                   float weight_threshold, uint32_t max_intersections,
                                   float *points_grad, void *diffuse_grad, void *specular_grad,
-                                  float *density_grad, void *point_error, uint32_t *err,
-                                  vt_stream stream)
+                                  float *density_grad, void *point_error, void *workspace,
+                                  uint64_t workspace_bytes, uint32_t *err, vt_stream stream)
 {
     vt::TrainCommon a;
     vt_status st = vt::fill_common(a, scene, rays, num_rays, start, num_quantiles, depth_quantiles,
                                    weight_threshold, max_intersections, err, "vt_trace_bwd");
+    if (st != VT_OK) return st;
+    VT_REQUIRE(res == 4 || res == 8, "vt_trace_bwd: res must be 4 or 8, got %d", res);
+    VT_REQUIRE(!workspace || (((uintptr_t)workspace & 255u) == 0 &&
+                              workspace_bytes >= vt_trace_bwd_workspace_bytes(scene->num_points, res)),
+               "vt_trace_bwd: workspace must be 256-byte aligned and vt_trace_bwd_workspace_bytes large");
     if (st != VT_OK) return st;
     VT_REQUIRE(diffuse && specular, "vt_trace_bwd: null textures");
     VT_REQUIRE(num_rays == 0 || (rgba && rgba_grad), "vt_trace_bwd: null rgba inputs");
@@ -262,16 +309,16 @@ extern "C" vt_status vt_trace_bwd(const vt_scene *scene, int attr_half, const vo
                             distortion, distortion_grad, W_total, S_total, points_grad,
                             (__half *)diffuse_grad, (__half *)specular_grad, density_grad,
                             (__half *)point_error};
-        if (res == 8) return vt::launch_bwd<__half, 8>(a, diffuse, specular, b, s);
-        if (res == 4) return vt::launch_bwd<__half, 4>(a, diffuse, specular, b, s);
+        if (res == 8) return vt::launch_bwd<__half, 8>(a, diffuse, specular, b, workspace, s);
+        if (res == 4) return vt::launch_bwd<__half, 4>(a, diffuse, specular, b, workspace, s);
     } else {
         vt::BwdIn<float> b{quantile_indices, (const float *)rgba, (const float *)rgba_grad,
                            depth_grad, (const float *)ray_error, contribution_alpha_grad,
                            distortion, distortion_grad, W_total, S_total, points_grad,
                            (float *)diffuse_grad, (float *)specular_grad, density_grad,
                            (float *)point_error};
-        if (res == 8) return vt::launch_bwd<float, 8>(a, diffuse, specular, b, s);
-        if (res == 4) return vt::launch_bwd<float, 4>(a, diffuse, specular, b, s);
+        if (res == 8) return vt::launch_bwd<float, 8>(a, diffuse, specular, b, workspace, s);
+        if (res == 4) return vt::launch_bwd<float, 4>(a, diffuse, specular, b, workspace, s);
     }
     return vt::set_error(VT_ERR_INVALID, "vt_trace_bwd: res must be 4 or 8, got %d", res);
 }

@@ -158,12 +158,33 @@ template <class AT, int R> struct BwdInteg {
     float W, S, Wt, St, dgr, Dt, Drun;
     float *pgrad;
     AT *ddiff, *dspec;
+    // Optional padded fp32 scratch: one float4 per texel / site, accumulated
+    // with vector atomics (1 instead of 3 per texel); null = scalar atomics
+    // straight into the outputs.
+    float4 *sdiff, *sspec, *spts;
     float *dden;
     AT *perr;
     V3 prev_geom, prev_grad, cur_grad, next_grad;
     uint32_t prev_idx;
 
     __device__ __forceinline__ uint32_t textured() const { return ntex; }
+
+    __device__ __forceinline__ void scatter4(float4 *g, uint32_t cell, const Bilin &b, V3 dl) const
+    {
+        float4 *base = g + (size_t)cell * (R * R);
+        atomicAdd(base + b.i00, make_float4(b.w00 * dl.x, b.w00 * dl.y, b.w00 * dl.z, 0.0f));
+        atomicAdd(base + b.i10, make_float4(b.w10 * dl.x, b.w10 * dl.y, b.w10 * dl.z, 0.0f));
+        atomicAdd(base + b.i01, make_float4(b.w01 * dl.x, b.w01 * dl.y, b.w01 * dl.z, 0.0f));
+        atomicAdd(base + b.i11, make_float4(b.w11 * dl.x, b.w11 * dl.y, b.w11 * dl.z, 0.0f));
+    }
+
+    __device__ __forceinline__ void add_site(uint32_t idx, V3 v) const
+    {
+        if (spts)
+            atomicAdd(spts + idx, make_float4(v.x, v.y, v.z, 0.0f));
+        else
+            atomic_add3(pgrad + (size_t)idx * 3, v);
+    }
 
     __device__ __forceinline__ void scatter(AT *g, uint32_t cell, const Bilin &b, V3 dl) const
     {
@@ -247,7 +268,7 @@ template <class AT, int R> struct BwdInteg {
         prev_grad = prev_grad + dLdt0 * g_prev;
         cur_grad = cur_grad + (dLdt0 * g0c + dLdt1 * g1c);
         next_grad = next_grad + dLdt1 * g1n;
-        if (prev_idx != 0xffffffffu) atomic_add3(pgrad + (size_t)prev_idx * 3, prev_grad);
+        if (prev_idx != 0xffffffffu) add_site(prev_idx, prev_grad);
         prev_geom = P;
         prev_idx = cell;
         prev_grad = cur_grad;
@@ -257,12 +278,17 @@ template <class AT, int R> struct BwdInteg {
         if (has_color) {
             V3 dl = mk((dLdrgb.x * rgb.x) * (1.0f - rgb.x), (dLdrgb.y * rgb.y) * (1.0f - rgb.y),
                        (dLdrgb.z * rgb.z) * (1.0f - rgb.z));
-            scatter(ddiff, cell, db, dl);
-            scatter(dspec, cell, spec, dl);
+            if (sdiff) {
+                scatter4(sdiff, cell, db, dl);
+                scatter4(sspec, cell, spec, dl);
+            } else {
+                scatter(ddiff, cell, db, dl);
+                scatter(dspec, cell, spec, dl);
+            }
         }
         atomicAdd(dden + cell, dLds);
         if (T < wt) {
-            atomic_add3(pgrad + (size_t)prev_idx * 3, prev_grad);
+            add_site(prev_idx, prev_grad);
             return false;
         }
         return true;

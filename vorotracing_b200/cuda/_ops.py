@@ -467,7 +467,8 @@ def trace_vorotracing_bwd(points, diffuse, specular, density, adjacency, offsets
                           start_point, rgb_out, rgb_grad_in, depth_quantiles, depth_indices,
                           depth_grad, ray_error, contribution_alpha_grad: float, distortion,
                           distortion_grad, W_total, S_total, t_far, weight_threshold: float,
-                          max_intersections: int, faces=None, grads=None):
+                          max_intersections: int, faces=None, grads=None,
+                          vector_atomics: bool = True):
     """Training backward (tracing_octmap.cu:860-1103).  Gradients go to new
     zeroed tensors, or accumulate into ``grads`` = (points, diffuse, specular,
     density) when given.  Returns the reference's 6-tuple (points_grad, diffuse_grad, specular_grad, density_grad, ray_grad,
@@ -559,6 +560,10 @@ def trace_vorotracing_bwd(points, diffuse, specular, density, adjacency, offsets
         faces = prefetch_faces(points, adjacency, offsets)
     scene = make_scene(points, density, offsets, faces)
     err = torch.zeros(1, dtype=torch.int32, device=dev)
+    ws, wsb = None, 0
+    if vector_atomics and nr:
+        wsb = int(lib().vt_trace_bwd_workspace_bytes(C.c_uint32(n), C.c_int(res)))
+        ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
     check(lib().vt_trace_bwd(C.byref(scene), C.c_int(half), ptr(diffuse), ptr(specular),
                              C.c_int(res), ptr(rays), C.c_uint32(nr), ptr(start_point),
                              C.c_uint32(K), ptr(dq), ptr(di), ptr(rgb_out), ptr(g), ptr(dg),
@@ -566,8 +571,8 @@ def trace_vorotracing_bwd(points, diffuse, specular, density, adjacency, offsets
                              ptr(ts["distortion"]), ptr(dgr), ptr(ts["W_total"]),
                              ptr(ts["S_total"]), C.c_float(weight_threshold),
                              C.c_uint32(max_intersections), ptr(points_grad), ptr(diffuse_grad),
-                             ptr(specular_grad), ptr(density_grad), ptr(perr), ptr(err),
-                             stream_ptr(dev)), "vt_trace_bwd")
+                             ptr(specular_grad), ptr(density_grad), ptr(perr), ptr(ws),
+                             C.c_uint64(wsb), ptr(err), stream_ptr(dev)), "vt_trace_bwd")
     if _CHECK_ERRORS:
         _check_err(err)
     return points_grad, diffuse_grad, specular_grad, density_grad, ray_grad, perr
