@@ -4,7 +4,8 @@
       views at 1296x840 sharded by view over the ranks (strong scaling:
       the 64 views are the fixed total).  Metric: Mrays/s, frames/s.
   C4  training step on a 3M-site fp32 scene: one 1552x1040 camera per rank
-      (orbit view = rank) against a seeded U(0,1) target image; a step is
+      (orbit view = rank, rays in 4x8 tile order) against a seeded U(0,1)
+      target image; a step is
       packed-face rebuild + forward + MSE gradient + backward + NCCL
       all-reduce of the flat fp32 gradient bucket (optimizer excluded).
       Metric: training rays/s (weak scaling).
@@ -125,9 +126,17 @@ def run_c4(args, ws, rank, dev):
     bvh = NNBVH()
     bvh.build(t["points"])
     st0 = bvh.query(t["points"], rays[0, 0, :3].reshape(1, 3))
-    start = st0.expand(H * W).reshape(H, W).contiguous().view(torch.uint32)
+    start = st0.expand(H * W).contiguous().view(torch.uint32)
     gen = torch.Generator(device=dev).manual_seed(1234 + rank)
     target = torch.rand((H, W, 3), generator=gen, device=dev)
+    # Batch order is free in training (the reference samples patch-coherent
+    # batches, vorotracing/datasets/datasets.py:238-241): rays and target go
+    # in 4x8 tile order so that a warp traces neighbouring pixels.
+    from vorotracing_b200.cuda import _ops as ops_
+
+    perm = ops_.tile_perm(H, W, device=dev).long()
+    rays = rays.reshape(-1, 6)[perm].contiguous()
+    target = target.reshape(-1, 3)[perm].contiguous()
     n = t["points"].size(0)
     bucket = GradBucket(n, t["diffuse"].size(1), dev)
     nr = H * W
@@ -138,7 +147,7 @@ def run_c4(args, ws, rank, dev):
             t["points"], t["diffuse"], t["specular"], t["density"], t["adj"], t["offs"], rays,
             start, None, WT, 1024, False, faces=faces)
         g = torch.zeros_like(rgba)
-        g[..., :3] = (2.0 / (nr * 3)) * (rgba[..., :3] - target)
+        g[:, :3] = (2.0 / (nr * 3)) * (rgba[:, :3] - target)
         bucket.zero_()
         _ops.trace_vorotracing_bwd(t["points"], t["diffuse"], t["specular"], t["density"],
                                    t["adj"], t["offs"], rays, start, rgba, g, None, None, None,
