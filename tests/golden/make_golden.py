@@ -10,11 +10,14 @@ define the layout transforms and the camera convention of the hot path:
   VoroTracingInfer._pad_3to4           vorotracing/vorotracing.py:505-512
   VoroTracingInfer._reorder_by_morton  vorotracing/vorotracing.py:514-571
   generate_camera_rays                 vorotracing/utils/__init__.py:85-130
+  write_foam (.foam V4 and V3)         scripts/export_for_viewer.py:146-216
+  VoroTracing.save_checkpoint          vorotracing/vorotracing.py:421-436
 
 The reference's compiled extension is replaced by a stub module (its import
 would JIT-compile CUDA code that cannot be built here); none of the functions
 above call into it except NNBVH.build, which the stub makes a no-op.
-Output: tests/golden/layout_golden.npz (committed).
+Outputs (committed): tests/golden/layout_golden.npz, and scene_v4.foam /
+scene_v3.foam with their inputs in foam_inputs.npz.
 """
 from __future__ import annotations
 
@@ -113,6 +116,66 @@ def main(root: str):
     out["cam_rays"] = vu.generate_camera_rays(K, T, 32, 24).numpy()
     np.savez_compressed(os.path.join(HERE, "layout_golden.npz"), **out)
     print("wrote", os.path.join(HERE, "layout_golden.npz"))
+    _foam_golden(root, vv)
+
+
+def _foam_golden(root: str, vv):
+    """Write .foam files with the reference exporter from a small seeded scene."""
+    ds = types.ModuleType("vorotracing.datasets.datasets")
+    ds.ColmapConfig = object
+    sys.modules["vorotracing.datasets.datasets"] = ds
+    sys.path.insert(0, os.path.join(root, "scripts"))
+    import export_for_viewer as ex
+
+    rng = np.random.default_rng(77)
+    n, R = 40, 4
+    pts = rng.uniform(-1, 1, (n, 3)).astype(np.float32)
+    counts = rng.integers(3, 9, n)
+    offs = np.concatenate([[0], np.cumsum(counts)]).astype(np.uint32)
+    adj = rng.integers(0, n, int(offs[-1]) + 32).astype(np.uint32)
+    dens = rng.uniform(0, 2, (n, 1)).astype(np.float32)
+    dif = rng.normal(size=(n, R * R * 4)).astype(np.float16)
+    spe = rng.normal(size=(n, R * R * 4)).astype(np.float16)
+    dif.reshape(n, -1, 4)[:, :, 3] = 0
+    spe.reshape(n, -1, 4)[:, :, 3] = 0
+    adj_diff = rng.normal(size=(adj.shape[0], 4)).astype(np.float16)
+    poses = rng.normal(size=(3, 3, 4)).astype(np.float32)
+
+    class Model:
+        pass
+
+    m = Model()
+    m.primal_points = torch.from_numpy(pts)
+    m.density = torch.from_numpy(dens)
+    m.diffuse_fp16 = torch.from_numpy(dif)
+    m.specular_fp16 = torch.from_numpy(spe)
+    m.point_adjacency = torch.from_numpy(adj.astype(np.int64))
+    m.point_adjacency_offsets = torch.from_numpy(offs.astype(np.int64))
+    m.adjacent_diff = torch.from_numpy(adj_diff)
+    cfg = vv.VoroTracingConfig(oct_map_res=R, spec_oct_map_res=R)
+    aabb = (pts.min(0), pts.max(0))
+    for version in (4, 3):
+        ex.write_foam(os.path.join(HERE, f"scene_v{version}.foam"), m, cfg, poses, aabb[0],
+                      aabb[1], 0.01, 1e-3, 512, include_specular=True, version=version)
+    ex.write_foam(os.path.join(HERE, "scene_v4_nospec.foam"), m, cfg, poses, aabb[0], aabb[1],
+                  0.01, 1e-3, 512, include_specular=False, version=4)
+    np.savez_compressed(os.path.join(HERE, "foam_inputs.npz"), points=pts, density=dens,
+                        diffuse=dif, specular=spe, adj=adj, offs=offs, adj_diff=adj_diff,
+                        poses=poses)
+    print("wrote .foam goldens")
+    # reference checkpoint of a 16-site scene (R=4), written by the model itself
+    cfg = vv.VoroTracingConfig(oct_map_res=4, spec_oct_map_res=4)
+    k = 16
+    model = vv.VoroTracing(cfg, torch.from_numpy(pts[:k]),
+                           points_diffuse=torch.from_numpy(rng.normal(size=(k, 48)).astype(np.float32)),
+                           points_specular=torch.from_numpy(rng.normal(size=(k, 48)).astype(np.float32)),
+                           points_density=torch.from_numpy(rng.normal(size=(k, 1)).astype(np.float32)),
+                           points_adjacency=torch.from_numpy(adj[:40].astype(np.int64) % k),
+                           points_adjacency_offsets=torch.from_numpy(
+                               np.minimum(np.arange(k + 1) * 2, 40).astype(np.int64)),
+                           device=torch.device("cpu"))
+    model.save_checkpoint(os.path.join(HERE, "checkpoint_ref.pt"))
+    print("wrote checkpoint golden")
 
 
 if __name__ == "__main__":
