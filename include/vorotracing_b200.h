@@ -108,6 +108,21 @@ VT_API vt_status vt_trace_infer_q8(const vt_scene *scene, const uint8_t *diffuse
                             float cell_skip_threshold, void *rgba, const vt_debug *debug,
                             uint32_t *err, vt_stream stream);
 
+/* Depth render (the viewer's depth modes, vorotracing/viewer.py:414-433; no
+ * kernel counterpart in the reference, which runs the full training forward
+ * with a per-ray copy of the thresholds).  thresholds: K transmittance
+ * levels shared by all rays, decreasing, device memory.  Training-forward
+ * transmittance rule, no colour.  depth (num_rays) f32 out, in ray order:
+ * VT_DEPTH_FIRST_QUANTILE the depth where T falls below thresholds[0];
+ * VT_DEPTH_MEAN the mean of the positive quantile depths; -1 where none. */
+#define VT_DEPTH_FIRST_QUANTILE 0
+#define VT_DEPTH_MEAN 1
+VT_API vt_status vt_trace_depth(const vt_scene *scene, const float *rays, uint32_t num_rays,
+                                const uint32_t *start, const uint32_t *ray_perm,
+                                const float *thresholds, uint32_t num_thresholds, int mode,
+                                float weight_threshold, uint32_t max_intersections,
+                                float *depth, uint32_t *err, vt_stream stream);
+
 /* ---- training ---- */
 
 /* Training forward (attr_half = 0: f32 attributes and rgba; 1: binary16).
@@ -170,6 +185,16 @@ typedef struct {
 
 /* rays (height, width, spp, 6) f32: origin, unit direction. */
 VT_API vt_status vt_raygen(const vt_camera *cam, float *rays, vt_stream stream);
+
+/* Fused Adam step over flat fp32 buffers laid out in four groups ending at
+ * group_ends[0..3] (= n), learning rates lrs[0..3], torch.optim.Adam's
+ * update; then values of group clamp_group (or none, -1) are clamped to at
+ * most clamp_max.  Replaces the reference's optimizer.step() + density
+ * clamp (vorotracing/trainer.py:258-265, 503-527). */
+VT_API vt_status vt_adam_step(float *params, const float *grads, float *exp_avg,
+                              float *exp_avg_sq, uint64_t n, const uint64_t *group_ends,
+                              const float *lrs, float beta1, float beta2, float eps,
+                              uint32_t step, int clamp_group, float clamp_max, vt_stream stream);
 
 /* ---- ray-origin cell lookup (nearest site) ---- */
 

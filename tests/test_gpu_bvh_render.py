@@ -75,3 +75,38 @@ def test_render_host_roundtrip(c1_scene, c1_rays):
     out = scene.render_host(host, weight_threshold=0.01)
     dev = scene.render(_dev(c1_rays), weight_threshold=0.01).cpu()
     assert torch.equal(out.view(torch.int16), dev.view(torch.int16))
+
+
+@pytest.mark.parametrize("mode", ["mean", "quantile"])
+def test_render_depth_matches_oracle(c1_scene, c1_rays, mode):
+    """Fused depth render vs the oracle's training forward with the same
+    thresholds for every ray, averaged as the reference viewer does."""
+    from vorotracing_b200.render import InferScene
+
+    s = c1_scene
+    scene = InferScene(_dev(s["points"]), _dev(s["density"]), _dev(s["adj"]), _dev(s["offs"]),
+                       _dev(s["diffuse"]), _dev(s["specular"]))
+    n = 6
+    thr = (np.linspace(1 - 1 / (2 * n), 1 / (2 * n), n) if mode == "mean"
+           else np.array([0.3])).astype(np.float32)
+    depth = scene.render_depth(_dev(c1_rays), mode=mode, thresholds=_dev(thr),
+                               weight_threshold=0.001).cpu().numpy().reshape(-1)
+    nr = c1_rays.shape[0] * c1_rays.shape[1]
+    start = oracle.nn_query(s["points"], c1_rays.reshape(-1, 6)[:1, :3])
+    S = oracle.Scene(s["points"], s["adj"], s["offs"], s["density"], s["diffuse"], s["specular"],
+                     oracle.ATTR_F32)
+    f = oracle.trace_fwd(S, c1_rays, np.full(nr, start[0], np.uint32),
+                         depth_quantiles=np.tile(thr, (nr, 1)), wt=0.001)
+    d = f["depth"]
+    if mode == "mean":
+        ref = np.full(nr, -1.0, np.float32)
+        for r in range(nr):
+            v = [x for x in d[r] if x > 0]
+            if v:
+                acc = np.float32(0)
+                for x in v:
+                    acc = np.float32(acc + np.float32(x))
+                ref[r] = acc / np.float32(len(v))
+    else:
+        ref = d[:, 0]
+    np.testing.assert_array_equal(depth, ref)

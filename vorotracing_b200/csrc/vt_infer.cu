@@ -165,3 +165,55 @@ extern "C" vt_status vt_trace_infer_q8(const vt_scene *scene, const uint8_t *dif
     }
     return vt::set_error(VT_ERR_INVALID, "vt_trace_infer_q8: res must be 4 or 8, got %d", res);
 }
+
+// ---------------------------------------------------------------- depth
+namespace vt {
+
+__global__ void __launch_bounds__(kInferBlock)
+    depth_kernel(InferArgs a, const float *__restrict__ thr, uint32_t K, int mode, float *out)
+{
+    uint32_t tid = blockIdx.x * blockDim.x + threadIdx.x;
+    if (tid >= a.num_rays) return;
+    uint32_t ray_id = a.perm ? __ldg(a.perm + tid) : tid;
+    if (ray_id >= a.num_rays) {
+        report(a.err, VT_ERR_DATA);
+        return;
+    }
+    Ray ray = load_ray(a.rays, ray_id);
+    uint32_t start = __ldg(a.start + ray_id);
+    if (start >= a.n_points) {
+        report(a.err, VT_ERR_DATA);
+        out[ray_id] = -1.0f;
+        return;
+    }
+    DepthInteg I(thr, K, a.wt);
+    walk<DepthInteg, false>(ray, a.faces, a.offs, a.points, a.density, start, a.max_steps, I,
+                            ray_id, a.dbg);
+    float v;
+    if (mode == VT_DEPTH_FIRST_QUANTILE)
+        v = I.qi > 0 ? I.first : -1.0f;
+    else
+        v = I.cnt ? I.sum / (float)I.cnt : -1.0f;
+    out[ray_id] = v;
+}
+
+}  // namespace vt
+
+extern "C" vt_status vt_trace_depth(const vt_scene *scene, const float *rays, uint32_t num_rays,
+                                    const uint32_t *start, const uint32_t *ray_perm,
+                                    const float *thresholds, uint32_t num_thresholds, int mode,
+                                    float weight_threshold, uint32_t max_intersections,
+                                    float *depth, uint32_t *err, vt_stream stream)
+{
+    vt::InferArgs a;
+    vt_status st = vt::fill_args(a, scene, rays, num_rays, start, ray_perm, weight_threshold,
+                                 max_intersections, 0.0f, depth, nullptr, err, "vt_trace_depth");
+    if (st != VT_OK) return st;
+    VT_REQUIRE(thresholds && num_thresholds > 0, "vt_trace_depth: thresholds required");
+    VT_REQUIRE(mode == VT_DEPTH_FIRST_QUANTILE || mode == VT_DEPTH_MEAN,
+               "vt_trace_depth: unknown mode %d", mode);
+    if (num_rays == 0) return VT_OK;
+    vt::depth_kernel<<<vt::grid_for(num_rays, vt::kInferBlock), vt::kInferBlock, 0,
+                       (cudaStream_t)stream>>>(a, thresholds, num_thresholds, mode, depth);
+    return vt::check_launch("depth_kernel");
+}

@@ -110,3 +110,47 @@ template <int R, class Tex> struct InferInteg {
 };
 
 }  // namespace vt
+
+namespace vt {
+
+// Depth-only integrator: the training forward's transmittance and depth-
+// quantile rule (ray_integrator_octmap.cuh:114-151: T advances in every
+// segment, depth_k = t0 + log(T / q_k) / density when T first drops below
+// q_k, continue while T > weight_threshold) without any colour work.  Used
+// for the viewer's depth modes (vorotracing/viewer.py:414-433): it returns
+// the first quantile's depth, or the mean of the positive quantile depths.
+struct DepthInteg {
+    const float *thr;  // K thresholds shared by all rays, decreasing
+    uint32_t K, qi;
+    float qv, wt, T, sum, first;
+    uint32_t cnt;
+
+    __device__ __forceinline__ DepthInteg(const float *thr_, uint32_t K_, float wt_)
+        : thr(thr_), K(K_), qi(0), qv(K_ ? thr_[0] : 0.0f), wt(wt_), T(1.0f), sum(0.0f),
+          first(-1.0f), cnt(0)
+    {
+    }
+
+    __device__ __forceinline__ uint32_t textured() const { return 0; }
+
+    __device__ __forceinline__ bool integrate(uint32_t, float t0, float t1, V3, V3, float s)
+    {
+        float delta = fmaxf(t1 - t0, 0.0f);
+        float alpha = 1.0f - expf_exact(-s * delta);
+        float nT = T * (1.0f - alpha);
+        while (qi < K && nT < qv) {
+            float d = t0 + logf_exact(T / qv) / s;
+            if (qi == 0) first = d;
+            if (d > 0.0f) {
+                sum += d;
+                cnt++;
+            }
+            qi++;
+            if (qi < K) qv = thr[qi];
+        }
+        T = nT;
+        return T > wt;
+    }
+};
+
+}  // namespace vt

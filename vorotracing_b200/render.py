@@ -97,6 +97,49 @@ class InferScene:
             self.adjacent_diff, ray_perm, weight_threshold, max_intersections,
             cell_skip_threshold, debug=debug)
 
+    def render_depth(self, rays, mode: str = "mean", n: int = 8, threshold: float = 0.5,
+                     start_point=None, weight_threshold=0.001, max_intersections=1024,
+                     use_warp_perm: bool = True, per_ray_start: bool = False,
+                     thresholds=None):
+        """Depth image (the viewer's depth modes, vorotracing/viewer.py:414-433).
+
+        mode "mean": mean of the depths at n transmittance levels
+        linspace(1 - 1/(2n), 1/(2n), n) over the positive ones; mode
+        "quantile": depth where transmittance falls below ``threshold``.
+        ``thresholds`` (K,) overrides the levels of either mode.
+        -1 where undefined.  Returns float32 of shape rays.shape[:-1]."""
+        import ctypes as C
+
+        from ._lib import check, lib, ptr, stream_ptr
+
+        dev = rays.device
+        if mode == "mean":
+            thr = torch.linspace(1 - 1 / (2 * n), 1 / (2 * n), n, device=dev)
+            m = 1
+        elif mode == "quantile":
+            thr = torch.full((1,), float(threshold), device=dev)
+            m = 0
+        else:
+            raise ValueError(f"unknown depth mode {mode!r}")
+        if thresholds is not None:
+            thr = torch.as_tensor(thresholds, dtype=torch.float32, device=dev).reshape(-1)
+        rays_c = rays.contiguous()
+        ray_perm = None
+        if use_warp_perm and rays.dim() == 3 and rays.shape[-1] == 6:
+            ray_perm = self.tile_perm(rays.shape[0], rays.shape[1])
+        if start_point is None:
+            start_point = self.get_starting_point(rays_c, per_ray_start)
+        start_point = torch.broadcast_to(start_point, rays.shape[:-1]).contiguous()
+        out = torch.empty(rays.shape[:-1], dtype=torch.float32, device=dev)
+        scene = _ops.make_scene(self.primal_points, self.density, self.point_adjacency_offsets,
+                                self.adjacent_diff)
+        check(lib().vt_trace_depth(C.byref(scene), ptr(rays_c), C.c_uint32(rays.numel() // 6),
+                                   ptr(start_point), ptr(ray_perm), ptr(thr),
+                                   C.c_uint32(thr.numel()), C.c_int(m),
+                                   C.c_float(weight_threshold), C.c_uint32(max_intersections),
+                                   ptr(out), None, stream_ptr(dev)), "vt_trace_depth")
+        return out
+
     def render_host(self, rays_host: torch.Tensor, out_host: torch.Tensor | None = None,
                     **kw) -> torch.Tensor:
         """End-to-end render of host rays (pinned memory recommended): copy in,
