@@ -99,17 +99,17 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def load_scene(rank: int, ws: int, name: str = "C2"):
-    """Scene arrays of a configuration; rank 0 builds the Delaunay cache first."""
+def load_scene(rank: int, ws: int, name: str = "C2", adjacency: str = "qhull"):
+    """Scene arrays of a configuration; rank 0 builds the adjacency cache first."""
     from vorotracing_b200 import scene as sc
 
     if ws > 1:
         import torch.distributed as dist
 
         if rank == 0:
-            sc.config_scene(name)
+            sc.config_scene(name, adjacency=adjacency)
         dist.barrier()
-    return sc.config_scene(name)
+    return sc.config_scene(name, adjacency=adjacency)
 
 
 def compulsory_bytes(scene, rays, start, dbg_ops):

@@ -15,6 +15,10 @@
       ray gets its own start cell from the BVH; pixel rows are dealt to the
       ranks in 4-row bands (strong scaling).  Metric: Mrays/s.
 
+Scenes: C2/C3 use scipy/Qhull adjacency (as the parity tests do); the 3M- and
+4M-site C4/C5 scenes are built with the GPU Voronoi builder (seconds instead
+of minutes of host time).
+
 Timing follows bench.py: CUDA events per step on the launching stream, L2
 flushed between steps, max over ranks, nvidia-smi clocks sampled meanwhile.
 """
@@ -117,7 +121,7 @@ def run_c3(args, ws, rank, dev):
 def run_c4(args, ws, rank, dev):
     from vorotracing_b200.cuda import _ops
 
-    s = bench.load_scene(rank, ws, "C4")
+    s = bench.load_scene(rank, ws, "C4", adjacency="gpu")
     t = _scene_tensors(s, dev)
     W, H = sc.CONFIGS["C4"]["W"], sc.CONFIGS["C4"]["H"]
     rays = torch.from_numpy(sc.pinhole_rays(sc.intrinsics(W, H), sc.orbit_pose(rank, 64), W, H)).to(dev)
@@ -174,7 +178,7 @@ def run_c5(args, ws, rank, dev):
     from vorotracing_b200.cameras import FISHEYE, ROLLING, THIN_LENS, Camera
     from vorotracing_b200.render import InferScene
 
-    s = bench.load_scene(rank, ws, "C5")
+    s = bench.load_scene(rank, ws, "C5", adjacency="gpu")
     t = _scene_tensors(s, dev)
     scene = InferScene(t["points"], t["density"], t["adj"], t["offs"], t["diffuse"],
                        t["specular"], quantize="fp16", sort_morton=True)

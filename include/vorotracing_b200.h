@@ -224,6 +224,24 @@ VT_API vt_status vt_bvh_query(const void *nodes, const float *points, uint32_t n
                               const float *queries, uint32_t num_queries, int32_t *out,
                               uint32_t *err, vt_stream stream);
 
+/* ---- Voronoi adjacency (replaces the external paragram package,
+ *      vorotracing/cuda/__init__.py:16-46) ---- */
+
+/* Scratch for vt_voronoi_adjacency / vt_voronoi_write (keep it between the two calls). */
+VT_API uint64_t vt_voronoi_bytes(uint32_t num_points);
+/* Voronoi face adjacency of the sites by per-cell clipping.  Writes the CSR
+ * offsets (num_points + 1, device) and returns the entry count on the host
+ * (*num_entries); neighbour ids of each row are ascending.  *unconverged
+ * (host, optional) = cells left empty after every pass.  Synchronises the
+ * stream (it reads sizes back to the host). */
+VT_API vt_status vt_voronoi_adjacency(const float *points, uint32_t num_points, void *workspace,
+                                      uint64_t workspace_bytes, uint32_t *offsets,
+                                      uint64_t *num_entries, uint32_t *unconverged,
+                                      vt_stream stream);
+/* Write the neighbour ids into adjacency (>= *num_entries entries). */
+VT_API vt_status vt_voronoi_write(const void *workspace, uint32_t num_points,
+                                  const uint32_t *offsets, uint32_t *adjacency, vt_stream stream);
+
 /* ---- layout transforms ---- */
 
 /* Column-wise min and max of a (rows, cols<=4) f32 matrix -> out[2*c], out[2*c+1].

@@ -576,3 +576,35 @@ def trace_vorotracing_bwd(points, diffuse, specular, density, adjacency, offsets
     if _CHECK_ERRORS:
         _check_err(err)
     return points_grad, diffuse_grad, specular_grad, density_grad, ray_grad, perr
+
+
+# ---------------------------------------------------------------- Voronoi adjacency
+
+def build_voronoi_adjacency(points, *, debug: bool = False, initial_guesses=None,
+                            initial_guesses_offsets=None, chunk_padding: int = 32):
+    """Voronoi CSR adjacency of the sites on the GPU (the reference's adapter
+    around paragram, vorotracing/cuda/__init__.py:16-46): returns (adjacency
+    uint32 with ``chunk_padding`` zero entries at the tail, offsets uint32
+    (N+1), status int32 tensor [cells left without neighbours]).
+    ``debug`` and the initial-guess arguments are accepted for signature
+    compatibility; the clipping method needs no initial guesses."""
+    del debug, initial_guesses, initial_guesses_offsets
+    pts = points.detach().contiguous()
+    if pts.device.type != "cuda" or pts.dtype != torch.float32 or pts.dim() != 2 or pts.size(1) != 3:
+        _fail("points must be a float32 (N, 3) CUDA tensor")
+    n = pts.size(0)
+    L = lib()
+    L.vt_voronoi_bytes.restype = C.c_uint64
+    wb = int(L.vt_voronoi_bytes(C.c_uint32(n)))
+    ws = _ws(wb, pts.device)
+    offs = torch.empty(n + 1, dtype=torch.int32, device=pts.device)
+    E = C.c_uint64(0)
+    bad = C.c_uint32(0)
+    stream = stream_ptr(pts.device)
+    check(L.vt_voronoi_adjacency(ptr(pts), C.c_uint32(n), ptr(ws), C.c_uint64(wb), ptr(offs),
+                                 C.byref(E), C.byref(bad), stream), "vt_voronoi_adjacency")
+    adj = torch.zeros(int(E.value) + chunk_padding, dtype=torch.int32, device=pts.device)
+    check(L.vt_voronoi_write(ptr(ws), C.c_uint32(n), ptr(offs), ptr(adj), stream),
+          "vt_voronoi_write")
+    status = torch.tensor([int(bad.value)], dtype=torch.int32)
+    return adj.view(torch.uint32), offs.view(torch.uint32), status

@@ -71,17 +71,31 @@ def _cache_path(tag: str) -> str:
     return os.path.join(root, tag + ".npz")
 
 
-def make_scene(n: int, seed: int, plane: bool, res: int, cache: bool = True) -> dict:
+def gpu_voronoi_csr(points: np.ndarray, pad: int = CSR_PAD):
+    """Voronoi adjacency built on the GPU (cuda.build_voronoi_adjacency)."""
+    import torch
+
+    from .cuda import build_voronoi_adjacency
+
+    adj, offs, _ = build_voronoi_adjacency(torch.from_numpy(np.ascontiguousarray(points)).cuda(),
+                                           chunk_padding=pad)
+    return adj.cpu().numpy(), offs.cpu().numpy()
+
+
+def make_scene(n: int, seed: int, plane: bool, res: int, cache: bool = True,
+               adjacency: str = "qhull") -> dict:
     """Sites, CSR and attributes.  Attributes are float32 logits:
-    diffuse U(0,1), specular U(-0.5,0.5) (N, 3R^2); density softplus(N(0,1)) (N, 1)."""
-    tag = hashlib.sha1(f"v1-{n}-{seed}-{plane}".encode()).hexdigest()[:16]
+    diffuse U(0,1), specular U(-0.5,0.5) (N, 3R^2); density softplus(N(0,1)) (N, 1).
+    adjacency: "qhull" (scipy Delaunay, the parity tests' scenes) or "gpu"
+    (the GPU clipping builder, seconds instead of minutes for millions of sites)."""
+    tag = hashlib.sha1(f"v1-{n}-{seed}-{plane}-{adjacency}".encode()).hexdigest()[:16]
     path = _cache_path(tag)
     if cache and os.path.exists(path):
         z = np.load(path)
         pts, adj, offs = z["points"], z["adj"], z["offs"]
     else:
         pts = make_sites(n, seed, plane)
-        adj, offs = delaunay_csr(pts)
+        adj, offs = delaunay_csr(pts) if adjacency == "qhull" else gpu_voronoi_csr(pts)
         if cache:
             np.savez(path, points=pts, adj=adj, offs=offs)
     rng = np.random.default_rng(seed + 1000)
@@ -101,9 +115,11 @@ CONFIGS = {
 }
 
 
-def config_scene(name: str, n: int | None = None, cache: bool = True) -> dict:
+def config_scene(name: str, n: int | None = None, cache: bool = True,
+                 adjacency: str = "qhull") -> dict:
     c = CONFIGS[name]
-    return make_scene(n or c["n"], c["seed"], c["plane"], c["res"], cache=cache)
+    return make_scene(n or c["n"], c["seed"], c["plane"], c["res"], cache=cache,
+                      adjacency=adjacency)
 
 
 # ---------------------------------------------------------------- cameras
