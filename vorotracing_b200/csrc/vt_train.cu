@@ -93,7 +93,7 @@ template <class AT> struct BwdIn {
     float4 *sdiff, *sspec, *spts;  // padded scratch or null
 };
 
-template <class AT, int R>
+template <class AT, int R, int F>
 __global__ void __launch_bounds__(kTrainBlock, VT_BWD_MIN_BLOCKS)
     bwd_kernel(TrainCommon a, TexPlain<AT, R> tex, BwdIn<AT> b)
 {
@@ -105,7 +105,7 @@ __global__ void __launch_bounds__(kTrainBlock, VT_BWD_MIN_BLOCKS)
         report(a.err, VT_ERR_DATA);
         return;
     }
-    BwdInteg<AT, R> I;
+    BwdInteg<AT, R, F> I;
     I.ray = ray;
     I.tex = tex;
     I.wt = a.wt;
@@ -125,7 +125,7 @@ __global__ void __launch_bounds__(kTrainBlock, VT_BWD_MIN_BLOCKS)
     I.g_a = g[3];
     I.ray_error = b.ray_error ? tof<AT>(b.ray_error[r]) : 0.0f;
     float cdg = 0.0f;
-    for (uint32_t i = 0; i < a.K; ++i) {
+    for (uint32_t i = 0; (F & kBwdDepth) != 0 && i < a.K; ++i) {
         uint32_t pi = b.qidx[(size_t)r * a.K + i];
         if (pi != 0xffffffffu) cdg += b.depth_grad[(size_t)r * a.K + i] / __ldg(a.density + pi);
     }
@@ -157,7 +157,7 @@ __global__ void __launch_bounds__(kTrainBlock, VT_BWD_MIN_BLOCKS)
     oct_encode<R>(mk(-ray.d.x, -ray.d.y, -ray.d.z), tu, tv);
     I.spec = make_bilin<R>(tu, tv);
     WalkDebug none{nullptr, 0, nullptr, nullptr, nullptr, nullptr};
-    walk<BwdInteg<AT, R>, false>(ray, a.faces, a.offs, a.points, a.density, start, a.max_steps, I,
+    walk<BwdInteg<AT, R, F>, false>(ray, a.faces, a.offs, a.points, a.density, start, a.max_steps, I,
                                  r, none);
 }
 
@@ -221,7 +221,18 @@ vt_status launch_bwd(const TrainCommon &a, const void *dif, const void *spe, Bwd
     } else {
         b.sdiff = b.sspec = b.spts = nullptr;
     }
-    bwd_kernel<AT, R><<<grid_for(a.num_rays, kTrainBlock), kTrainBlock, 0, s>>>(a, t, b);
+    const int F = (a.K > 0 && a.dq ? kBwdDepth : 0) | (b.dist_grad ? kBwdDist : 0) |
+                  (b.ray_error && b.point_error ? kBwdErr : 0);
+    const unsigned g = grid_for(a.num_rays, kTrainBlock);
+    switch (F) {
+#define VT_BWD_CASE(f)                                                                             \
+    case f:                                                                                        \
+        bwd_kernel<AT, R, f><<<g, kTrainBlock, 0, s>>>(a, t, b);                                   \
+        break;
+        VT_BWD_CASE(0) VT_BWD_CASE(1) VT_BWD_CASE(2) VT_BWD_CASE(3)
+        VT_BWD_CASE(4) VT_BWD_CASE(5) VT_BWD_CASE(6) VT_BWD_CASE(7)
+#undef VT_BWD_CASE
+    }
     if (ws) {
         compact4_kernel<AT><<<grid_for(ntex, 256), 256, 0, s>>>(b.sdiff, ntex, b.diffuse_grad);
         compact4_kernel<AT><<<grid_for(ntex, 256), 256, 0, s>>>(b.sspec, ntex, b.specular_grad);

@@ -141,7 +141,13 @@ __device__ __forceinline__ void atomic_add3(float *p, V3 v)
     atomicAdd(p + 2, v.z);
 }
 
-template <class AT, int R> struct BwdInteg {
+// Feature switches of the backward (compile time): the common training step
+// has none of them, and their per-ray state then costs no registers.
+constexpr int kBwdDepth = 1;  // depth-quantile gradients
+constexpr int kBwdDist = 2;   // distortion-loss gradient
+constexpr int kBwdErr = 4;    // per-cell point_error accumulation
+
+template <class AT, int R, int F = kBwdDepth | kBwdDist | kBwdErr> struct BwdInteg {
     Ray ray;
     TexPlain<AT, R> tex;
     Bilin spec;
@@ -220,7 +226,8 @@ template <class AT, int R> struct BwdInteg {
         float dadd = 0.0f;
         if (delta > 0.0f) dadd = s * (1.0f - alpha);
         acc = acc + w * rgb;
-        if (perr) atomic_add<AT>(perr + cell, w * ray_error);
+        if constexpr ((F & kBwdErr) != 0)
+            if (perr) atomic_add<AT>(perr + cell, w * ray_error);
         V3 dLdrgb = mk(g_rgb.x * w, g_rgb.y * w, g_rgb.z * w);
         V3 rest = divs(fwd_rgb - acc, T * ((1.0f - alpha) + 1e-6f));
         float dLda = T * dot(rgb - rest, g_rgb);
@@ -228,7 +235,7 @@ template <class AT, int R> struct BwdInteg {
         float dLds = dLda * dads;
         float dLddt = dLda * dadd;
         float dLdt0 = 0.0f;
-        if (dgr != 0.0f) {
+        if ((F & kBwdDist) != 0 && dgr != 0.0f) {
             float s0 = 1.0f - 1.0f / (1.0f + t0);
             float s1 = 1.0f - 1.0f / (1.0f + t1);
             float mid = 0.5f * (s0 + s1);
@@ -246,7 +253,7 @@ template <class AT, int R> struct BwdInteg {
             S += w * mid;
         }
         float nT = T * (1.0f - alpha);
-        while (qi < K && nT < qv) {
+        while ((F & kBwdDepth) != 0 && qi < K && nT < qv) {
             float gi = dgrad[qi] / s;
             dLdt0 += gi;
             dLds += ((-gi) * logf_exact(T / qv)) / s;
@@ -254,7 +261,7 @@ template <class AT, int R> struct BwdInteg {
             qi++;
             if (qi < K) qv = qthr[qi];
         }
-        if (qi < K) {
+        if ((F & kBwdDepth) != 0 && qi < K) {
             dLds += (-delta) * cur_dg;
             dLddt += (-s) * cur_dg;
         }
