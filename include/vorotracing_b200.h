@@ -52,6 +52,13 @@ typedef struct CUstream_st *vt_stream; /* == cudaStream_t */
 VT_API const char *vt_last_error(void);
 /* Library version, e.g. "0.1.0". */
 VT_API const char *vt_version(void);
+/* Device address of page-locked host memory (cudaHostAlloc / cudaHostRegister
+ * with mapping; every such allocation is mapped under unified addressing).
+ * The trace entry points accept it for rays and rgba, so that a kernel reads
+ * its rays from and writes its pixels to host memory over the bus while it
+ * runs (zero-copy end-to-end render).  No reference counterpart: the
+ * reference's operators take device tensors only. */
+VT_API vt_status vt_host_device_ptr(const void *host, void **device);
 
 /* Scene in device memory.  points (N,3) f32, density (N) f32, offsets (N+1)
  * u32 CSR, faces = packed face rows written by vt_prefetch_adj. */

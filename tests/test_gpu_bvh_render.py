@@ -65,16 +65,21 @@ def test_infer_scene_matches_oracle(c1_scene, c1_rays, quant):
                                   ref["rgba"].view(np.uint16))
 
 
-def test_render_host_roundtrip(c1_scene, c1_rays):
+@pytest.mark.parametrize("transfer,bands", [("zero_copy", 1), ("bands", 1), ("bands", 3),
+                                            ("bands", 4), ("bands", 7)])
+def test_render_host_roundtrip(c1_scene, c1_rays, transfer, bands):
     from vorotracing_b200.render import InferScene
 
     s = c1_scene
     scene = InferScene(_dev(s["points"]), _dev(s["density"]), _dev(s["adj"]), _dev(s["offs"]),
                        _dev(s["diffuse"]), _dev(s["specular"]))
     host = torch.from_numpy(c1_rays).pin_memory()
-    out = scene.render_host(host, weight_threshold=0.01)
+    out = scene.render_host(host, transfer=transfer, bands=bands, weight_threshold=0.01)
     dev = scene.render(_dev(c1_rays), weight_threshold=0.01).cpu()
     assert torch.equal(out.view(torch.int16), dev.view(torch.int16))
+    # a second call reuses the device ray buffer; odd row counts leave a short last band
+    out2 = scene.render_host(host[:-5].clone().pin_memory(), transfer=transfer, bands=bands, weight_threshold=0.01)
+    assert torch.equal(out2.view(torch.int16), dev[:-5].view(torch.int16))
 
 
 @pytest.mark.parametrize("mode", ["mean", "quantile"])

@@ -44,6 +44,13 @@ def validate_scene_data(points, attributes, adjacency, offsets):
         _fail("point_adjacency must be on CUDA device")
 
 
+def host_device_ptr(t: torch.Tensor):
+    """Device address of a page-locked host tensor (vt_host_device_ptr)."""
+    out = C.c_void_p()
+    check(lib().vt_host_device_ptr(C.c_void_p(t.data_ptr()), C.byref(out)), "vt_host_device_ptr")
+    return out
+
+
 def _aligned(t: torch.Tensor, align: int) -> torch.Tensor:
     t = t.contiguous()
     if t.numel() and t.data_ptr() % align:
@@ -104,15 +111,19 @@ def _res_from(attr: torch.Tensor, channels: int) -> int:
 def trace_vorotracing_infer(points, diffuse, specular, density, adjacency, offsets, rays,
                             start_point, adjacent_diff, ray_perm, weight_threshold: float,
                             max_intersections: int, cell_skip_threshold: float,
-                            debug: dict | None = None):
-    """fp16 inference (tracing_octmap.cu:642-717).  Returns rgba (..., 4) float16."""
+                            debug: dict | None = None, out=None, host_io: bool = False):
+    """fp16 inference (tracing_octmap.cu:642-717).  Returns rgba (..., 4) float16.
+
+    host_io=True (an extension of this package): ``rays`` and ``out`` are
+    page-locked host tensors that the kernel reads and writes directly over
+    the bus (zero-copy); everything else stays on the device."""
     points = points.contiguous()
     diffuse = _aligned(diffuse, 8)
     specular = _aligned(specular, 8)
     density = density.contiguous()
     adjacency = adjacency.contiguous()
     offsets = offsets.contiguous()
-    rays = _aligned(rays, 8)
+    rays = rays if host_io else _aligned(rays, 8)
     start_point = start_point.contiguous()
     validate_scene_data(points, diffuse, adjacency, offsets)
     if diffuse.dtype != torch.float16:
@@ -127,14 +138,14 @@ def trace_vorotracing_infer(points, diffuse, specular, density, adjacency, offse
         _fail("start_point must have uint32 dtype")
     return _infer_common(points, diffuse, specular, density, adjacency, offsets, rays,
                          start_point, adjacent_diff, ray_perm, weight_threshold,
-                         max_intersections, cell_skip_threshold, None, debug)
+                         max_intersections, cell_skip_threshold, None, debug, out, host_io)
 
 
 def trace_vorotracing_infer_q8(points, diffuse, specular, density, adjacency, offsets, rays,
                                start_point, adjacent_diff, diff_scale, diff_offset, spec_scale,
                                spec_offset, weight_threshold: float, max_intersections: int,
                                cell_skip_threshold: float, ray_perm=None,
-                               debug: dict | None = None):
+                               debug: dict | None = None, out=None, host_io: bool = False):
     """q8 inference (tracing_octmap.cu:781-854).  Returns rgba (..., 4) float16."""
     points = points.contiguous()
     diffuse = diffuse.contiguous()
@@ -142,7 +153,7 @@ def trace_vorotracing_infer_q8(points, diffuse, specular, density, adjacency, of
     density = density.contiguous()
     adjacency = adjacency.contiguous()
     offsets = offsets.contiguous()
-    rays = _aligned(rays, 8)
+    rays = rays if host_io else _aligned(rays, 8)
     start_point = start_point.contiguous()
     validate_scene_data(points, diffuse, adjacency, offsets)
     if diffuse.dtype != torch.uint8:
@@ -152,14 +163,20 @@ def trace_vorotracing_infer_q8(points, diffuse, specular, density, adjacency, of
     q8 = (float(diff_scale), float(diff_offset), float(spec_scale), float(spec_offset))
     return _infer_common(points, diffuse, specular, density, adjacency, offsets, rays,
                          start_point, adjacent_diff, ray_perm, weight_threshold,
-                         max_intersections, cell_skip_threshold, q8, debug)
+                         max_intersections, cell_skip_threshold, q8, debug, out, host_io)
 
 
 def _infer_common(points, diffuse, specular, density, adjacency, offsets, rays, start_point,
-                  adjacent_diff, ray_perm, wt, max_int, skip, q8, debug):
+                  adjacent_diff, ray_perm, wt, max_int, skip, q8, debug, out=None,
+                  host_io=False):
     if rays.size(-1) != 6:
         _fail("rays must have 6 as the last dimension")
-    if rays.device.type != "cuda":
+    if host_io:
+        if not (rays.is_pinned() and rays.is_contiguous() and rays.data_ptr() % 8 == 0):
+            _fail("host_io rays must be contiguous, 8-byte aligned page-locked host memory")
+        if out is None or not (out.is_pinned() and out.is_contiguous()):
+            _fail("host_io needs a contiguous page-locked host out tensor")
+    elif rays.device.type != "cuda":
         _fail("rays must be on CUDA device")
     nr = rays.numel() // 6
     if start_point.numel() != nr:
@@ -178,22 +195,35 @@ def _infer_common(points, diffuse, specular, density, adjacency, offsets, rays, 
             _fail("ray_perm must be empty or have one entry per ray")
         if perm.dtype not in (torch.int32, torch.uint32):
             _fail("ray_perm must have int32 or uint32 dtype")
-    rgba = torch.empty(tuple(rays.shape[:-1]) + (4,), dtype=torch.float16, device=rays.device)
-    err = torch.zeros(1, dtype=torch.int32, device=rays.device)
+    shape = tuple(rays.shape[:-1]) + (4,)
+    dev = points.device
+    if out is not None:
+        if tuple(out.shape) != shape or out.dtype != torch.float16 or not out.is_contiguous():
+            _fail("out must be a contiguous float16 tensor of shape rays.shape[:-1] + (4,)")
+        rgba = out
+    else:
+        rgba = torch.empty(shape, dtype=torch.float16, device=dev)
+    if host_io:
+        rays_p, rgba_p = host_device_ptr(rays), host_device_ptr(rgba)
+    else:
+        if rgba.device != rays.device:
+            _fail("out must be on the rays' device")
+        rays_p, rgba_p = ptr(rays), ptr(rgba)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
     scene = make_scene(points, density, offsets, adjacent_diff)
     dbg, keep = _debug_struct(debug, nr, n)
     L = lib()
-    stream = stream_ptr(rays.device)
+    stream = stream_ptr(dev)
     if q8 is None:
         st = L.vt_trace_infer_f16(C.byref(scene), ptr(diffuse), ptr(specular), C.c_int(res),
-                                  ptr(rays), C.c_uint32(nr), ptr(start_point), ptr(perm),
+                                  rays_p, C.c_uint32(nr), ptr(start_point), ptr(perm),
                                   C.c_float(wt), C.c_uint32(max_int), C.c_float(skip),
-                                  ptr(rgba), dbg, ptr(err), stream)
+                                  rgba_p, dbg, ptr(err), stream)
     else:
         st = L.vt_trace_infer_q8(C.byref(scene), ptr(diffuse), ptr(specular), C.c_int(res),
-                                 *[C.c_float(v) for v in q8], ptr(rays), C.c_uint32(nr),
+                                 *[C.c_float(v) for v in q8], rays_p, C.c_uint32(nr),
                                  ptr(start_point), ptr(perm), C.c_float(wt), C.c_uint32(max_int),
-                                 C.c_float(skip), ptr(rgba), dbg, ptr(err), stream)
+                                 C.c_float(skip), rgba_p, dbg, ptr(err), stream)
     check(st, "trace infer")
     if debug is not None or _CHECK_ERRORS:
         _check_err(err)

@@ -76,7 +76,7 @@ class InferScene:
 
     def render(self, rays, start_point=None, weight_threshold=0.001, max_intersections=1024,
                cell_skip_threshold=0.0, use_warp_perm: bool = True, per_ray_start: bool = False,
-               debug=None):
+               debug=None, out=None, host_io: bool = False):
         ray_perm = None
         if use_warp_perm and rays.dim() == 3 and rays.shape[-1] == 6:
             ray_perm = self.tile_perm(rays.shape[0], rays.shape[1])
@@ -90,12 +90,12 @@ class InferScene:
                 self.point_adjacency, self.point_adjacency_offsets, rays, start_point,
                 self.adjacent_diff, self.diff_scale, self.diff_offset, self.spec_scale,
                 self.spec_offset, weight_threshold, max_intersections, cell_skip_threshold,
-                ray_perm=ray_perm, debug=debug)
+                ray_perm=ray_perm, debug=debug, out=out, host_io=host_io)
         return _ops.trace_vorotracing_infer(
             self.primal_points, self.diffuse_fp16, self.specular_fp16, self.density,
             self.point_adjacency, self.point_adjacency_offsets, rays, start_point,
             self.adjacent_diff, ray_perm, weight_threshold, max_intersections,
-            cell_skip_threshold, debug=debug)
+            cell_skip_threshold, debug=debug, out=out, host_io=host_io)
 
     def render_depth(self, rays, mode: str = "mean", n: int = 8, threshold: float = 0.5,
                      start_point=None, weight_threshold=0.001, max_intersections=1024,
@@ -141,13 +141,95 @@ class InferScene:
         return out
 
     def render_host(self, rays_host: torch.Tensor, out_host: torch.Tensor | None = None,
+                    transfer: Literal["zero_copy", "bands"] = "zero_copy", bands: int = 4,
+                    sync: bool = True, start_point=None, per_ray_start: bool = False,
                     **kw) -> torch.Tensor:
-        """End-to-end render of host rays (pinned memory recommended): copy in,
-        trace, copy the float16 rgba back.  Returns the host tensor."""
-        rays = rays_host.to(self.primal_points.device, non_blocking=True)
-        rgba = self.render(rays, **kw)
+        """End-to-end render of host rays: rays in, float16 rgba back in host
+        memory.  Returns the host tensor.
+
+        transfer="zero_copy" (default; ``rays_host`` must be page-locked): one
+        trace launch reads each ray from host memory over the bus and writes
+        its pixel straight back, so the 24 + 8 bytes per ray cross the bus
+        while the walk runs instead of before and after it.
+        transfer="bands": copies in row bands (heights a multiple of 4, so the
+        4x8 warp tiles stay whole) on two copy streams, band i+1's upload and
+        band i-1's download overlapping band i's trace.
+        Rays are independent, so both equal the device render bit for bit.
+        The start cell is the frame's first ray's cell (the reference's
+        broadcast, vorotracing.py:585-604) unless ``start_point`` or
+        ``per_ray_start`` is given; the first ray's origin is the only part
+        copied ahead.  With ``sync=False`` the call returns once the work is
+        queued and the current stream is ordered after it, so an event
+        recorded there afterwards marks completion."""
+        dev = self.primal_points.device
+        cur = torch.cuda.current_stream(dev)
         if out_host is None:
-            out_host = torch.empty(rgba.shape, dtype=rgba.dtype, pin_memory=True)
-        out_host.copy_(rgba, non_blocking=True)
-        torch.cuda.current_stream().synchronize()
+            out_host = torch.empty(tuple(rays_host.shape[:-1]) + (4,), dtype=torch.float16,
+                                   pin_memory=True)
+        if transfer == "zero_copy":
+            if not rays_host.is_pinned():
+                rays_host = rays_host.contiguous().pin_memory()
+            if per_ray_start and start_point is None:
+                rays_dev = rays_host.to(dev, non_blocking=True)
+                start_point = self.get_starting_point(rays_dev, per_ray=True)
+            elif start_point is None:
+                first = rays_host.reshape(-1, rays_host.shape[-1])[:1].to(dev, non_blocking=True)
+                start_point = self.get_starting_point(first).reshape(
+                    (1,) * (rays_host.dim() - 1))
+            self.render(rays_host, start_point=start_point, out=out_host, host_io=True, **kw)
+            if sync:
+                cur.synchronize()
+            return out_host
+        if transfer != "bands":
+            raise ValueError(f"unknown transfer mode {transfer!r}")
+        if rays_host.dim() != 3 or bands <= 1 or rays_host.shape[0] < 8:
+            rays = rays_host.to(dev, non_blocking=True)
+            rgba = self.render(rays, start_point=start_point, per_ray_start=per_ray_start, **kw)
+            out_host.copy_(rgba, non_blocking=True)
+            if sync:
+                cur.synchronize()
+            return out_host
+        H = rays_host.shape[0]
+        bh = -(-H // (bands * 4)) * 4
+        cuts = [(y, min(y + bh, H)) for y in range(0, H, bh)]
+        key = (tuple(rays_host.shape), dev)
+        if getattr(self, "_host_key", None) != key:
+            self._host_key = key
+            self._host_rays = torch.empty(rays_host.shape, dtype=torch.float32, device=dev)
+            self._h2d = torch.cuda.Stream(dev)
+            self._d2h = torch.cuda.Stream(dev)
+        rays_dev, h2d, d2h = self._host_rays, self._h2d, self._d2h
+        h2d.wait_stream(cur)  # the previous call's traces may still read rays_dev
+        d2h.wait_stream(cur)
+        ev_in = []
+        with torch.cuda.stream(h2d):
+            for y0, y1 in cuts:
+                rays_dev[y0:y1].copy_(rays_host[y0:y1], non_blocking=True)
+                e = torch.cuda.Event()
+                e.record(h2d)
+                ev_in.append(e)
+        keep = []
+        for (y0, y1), e in zip(cuts, ev_in):
+            cur.wait_event(e)
+            band = rays_dev[y0:y1]
+            if start_point is not None:
+                sp = torch.broadcast_to(start_point, rays_host.shape[:-1])[y0:y1]
+            elif per_ray_start:
+                sp = self.get_starting_point(band, per_ray=True)
+            else:
+                if y0 == 0:
+                    first = self.get_starting_point(band[:1, :1])
+                sp = first.reshape(1, 1).expand(y1 - y0, band.shape[1])
+            rgba = self.render(band, start_point=sp, **kw)
+            done = torch.cuda.Event()
+            done.record(cur)
+            d2h.wait_event(done)
+            with torch.cuda.stream(d2h):
+                out_host[y0:y1].copy_(rgba, non_blocking=True)
+            keep.append(rgba)
+        cur.wait_stream(d2h)
+        for t in keep:  # freed on the current stream only after the downloads
+            t.record_stream(d2h)
+        if sync:
+            cur.synchronize()
         return out_host
