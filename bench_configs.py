@@ -144,19 +144,22 @@ def run_c4(args, ws, rank, dev):
     n = t["points"].size(0)
     bucket = GradBucket(n, t["diffuse"].size(1), dev)
     nr = H * W
+    # the forward records each ray's first 256 cells; the backward replays
+    # them without scanning faces (1 KB per ray)
+    path = ops_.PathRecord(nr, 256, dev)
 
     def step():
         faces = _ops.prefetch_faces(t["points"], t["adj"], t["offs"])
         rgba, _, _, _, _, dist_, Wt, St, tfar = _ops.trace_vorotracing_fwd(
             t["points"], t["diffuse"], t["specular"], t["density"], t["adj"], t["offs"], rays,
-            start, None, WT, 1024, False, faces=faces)
+            start, None, WT, 1024, False, faces=faces, path=path)
         g = torch.zeros_like(rgba)
         g[:, :3] = (2.0 / (nr * 3)) * (rgba[:, :3] - target)
         bucket.zero_()
         _ops.trace_vorotracing_bwd(t["points"], t["diffuse"], t["specular"], t["density"],
                                    t["adj"], t["offs"], rays, start, rgba, g, None, None, None,
                                    None, 0.0, dist_, None, Wt, St, tfar, WT, 1024, faces=faces,
-                                   grads=bucket.views())
+                                   grads=bucket.views(), path=path)
         bucket.allreduce_()
 
     ms, clocks = Timer(args, dev).run(step, ws)
@@ -165,7 +168,8 @@ def run_c4(args, ws, rank, dev):
         _line(args, ws, "training rays/s, fwd+bwd+grad all-reduce, 3M-site scene, 1552x1040 per GPU (C4)",
               rays_total / (ms * 1e-3), "rays/s", ms, clocks,
               {"workload": "C4: 3M-site fp32 scene, R=8, one 1552x1040 camera per GPU vs a "
-                           "seeded U(0,1) target, MSE; step = face pack + fwd + bwd + NCCL "
+                           "seeded U(0,1) target, MSE; step = face pack + fwd (recording each "
+                           "ray's first 256 cells) + bwd (replaying them) + NCCL "
                            "all-reduce of the flat fp32 gradient bucket; optimizer excluded",
                "sites": n, "rays_per_step_per_gpu": nr,
                "grad_bucket_bytes": bucket.nbytes,

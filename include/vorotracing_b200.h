@@ -132,12 +132,27 @@ VT_API vt_status vt_trace_depth(const vt_scene *scene, const float *rays, uint32
 
 /* ---- training ---- */
 
+/* Path record: the training forward stores, for each ray, the cell it enters
+ * at every walk step (cells (cap, num_rays) u32, slot-major: cells[k *
+ * num_rays + r]) and the number of steps that found an exit face (len
+ * (num_rays) u32; steps beyond cap are not stored).  Given the same record,
+ * the backward enters the recorded cells without scanning their faces and
+ * resumes the face scan after the last stored step, with results identical
+ * to a backward without the record.  The record is only valid for the scene,
+ * rays, start cells and max_intersections of the forward that wrote it.  No
+ * reference counterpart (the reference's backward re-walks every ray). */
+typedef struct {
+    uint32_t *cells;
+    uint32_t cap;
+    uint32_t *len;
+} vt_path;
+
 /* Training forward (attr_half = 0: f32 attributes and rgba; 1: binary16).
  * diffuse/specular (N, 3*res*res).  depth_quantiles (num_rays, K) f32 or null
  * (K = 0); quantile_depths / quantile_indices (num_rays, K) out, unfilled
  * entries -1 / 0xffffffff.  contribution (N) in the attribute dtype,
  * zero-initialised by the caller, or null.  distortion, W_total, S_total,
- * t_far (num_rays) f32 out. */
+ * t_far (num_rays) f32 out.  path: null, or a record to write (vt_path). */
 VT_API vt_status vt_trace_fwd(const vt_scene *scene, int attr_half, const void *diffuse,
                               const void *specular, int res, const float *rays, uint32_t num_rays,
                               const uint32_t *start, uint32_t num_quantiles,
@@ -145,13 +160,14 @@ VT_API vt_status vt_trace_fwd(const vt_scene *scene, int attr_half, const void *
                               uint32_t max_intersections, void *rgba, float *quantile_depths,
                               uint32_t *quantile_indices, uint32_t *num_intersections,
                               void *contribution, float *distortion, float *W_total,
-                              float *S_total, float *t_far, const vt_debug *debug, uint32_t *err,
-                              vt_stream stream);
+                              float *S_total, float *t_far, const vt_debug *debug,
+                              const vt_path *path, uint32_t *err, vt_stream stream);
 
 /* Training backward.  Gradient outputs must be zero-initialised by the
  * caller: points_grad (N,3) f32, diffuse/specular_grad in the attribute
  * dtype, density_grad (N) f32, point_error (N) attribute dtype or null
- * (accumulated only when ray_error is given). */
+ * (accumulated only when ray_error is given).  path: null (walk every ray),
+ * or the record written by the matching forward. */
 VT_API vt_status vt_trace_bwd(const vt_scene *scene, int attr_half, const void *diffuse,
                               const void *specular, int res, const float *rays, uint32_t num_rays,
                               const uint32_t *start, uint32_t num_quantiles,
@@ -162,8 +178,8 @@ VT_API vt_status vt_trace_bwd(const vt_scene *scene, int attr_half, const void *
                               const float *W_total, const float *S_total, float weight_threshold,
                               uint32_t max_intersections, float *points_grad, void *diffuse_grad,
                               void *specular_grad, float *density_grad, void *point_error,
-                              void *workspace, uint64_t workspace_bytes, uint32_t *err,
-                              vt_stream stream);
+                              void *workspace, uint64_t workspace_bytes, const vt_path *path,
+                              uint32_t *err, vt_stream stream);
 /* Optional scratch of vt_trace_bwd (256-byte aligned): with it the texel and
  * site gradients accumulate in padded fp32 rows with one vector atomic per
  * texel (instead of three scalar atomics) and are added to the outputs at the

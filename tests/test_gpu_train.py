@@ -90,7 +90,10 @@ def test_fwd_matches_oracle(c1_scene, c1_rays, half):
 
 @pytest.mark.parametrize("half", [False, True])
 @pytest.mark.parametrize("with_extras", [False, True])
-def test_bwd_matches_oracle(c1_scene, c1_rays, half, with_extras):
+@pytest.mark.parametrize("path_cap", [None, 1, 7, 1024])
+def test_bwd_matches_oracle(c1_scene, c1_rays, half, with_extras, path_cap):
+    """path_cap: the backward replays the forward's path record (cap steps
+    per ray, the face scan resuming after them) instead of walking."""
     from vorotracing_b200.cuda import _ops
 
     s = c1_scene
@@ -113,12 +116,18 @@ def test_bwd_matches_oracle(c1_scene, c1_rays, half, with_extras):
                            wt=0.01, **{k: v for k, v in kw.items() if k != "distortion"},
                            distortion=f["distortion"])
     t = lambda a: None if a is None else _dev(a)
+    path = None
+    if path_cap is not None:
+        path = _ops.PathRecord(nr, path_cap, "cuda")
+        _ops.trace_vorotracing_fwd(g["points"], g["diffuse"], g["specular"], g["density"],
+                                   g["adj"], g["offs"], _dev(rays), _dev(start), t(dq), 0.01, 1024,
+                                   False, path=path)
     res = _ops.trace_vorotracing_bwd(
         g["points"], g["diffuse"], g["specular"], g["density"], g["adj"], g["offs"], _dev(rays),
         _dev(start), _dev(rgba), _dev(grgba), t(dq), t(kw.get("depth_idx")),
         t(kw.get("depth_grad")), t(kw.get("ray_error")), kw.get("contribution_alpha_grad", 0.0),
         _dev(f["distortion"]), t(kw.get("distortion_grad")), _dev(f["W"]), _dev(f["S"]),
-        _dev(f["t_far"]), 0.01, 1024)
+        _dev(f["t_far"]), 0.01, 1024, path=path)
     torch.cuda.synchronize()
     pg, dg, sg, deng, _, perr = res
     # fp16 attributes: the texel / point-error gradients are accumulated with
@@ -216,3 +225,32 @@ def test_bwd_vector_atomics_match_scalar(c1_scene, c1_rays, half):
     for x, y, name in zip(a[:4], b[:4], ("points", "diffuse", "specular", "density")):
         tol, frac = (1e-1, 2e-2) if half and name in ("diffuse", "specular") else (1e-3, 1e-4)
         _close(x.float().cpu().numpy(), y.float().cpu().numpy(), tol, frac, name)
+
+
+@pytest.mark.parametrize("cap", [1, 5, 1024])
+def test_path_record_is_the_cell_sequence(c1_scene, c1_rays, cap):
+    """The forward's path record holds the cells entered at each step (the
+    visited-cell sequence shifted by one) and the number of exit faces found."""
+    from vorotracing_b200.cuda import _ops
+
+    s = c1_scene
+    rays = c1_rays[::2, ::2].reshape(-1, 6)
+    nr = rays.shape[0]
+    S, start, g = _setup(s, rays, False)
+    args = (g["points"], g["diffuse"], g["specular"], g["density"], g["adj"], g["offs"],
+            _dev(rays), _dev(start))
+    path = _ops.PathRecord(nr, cap, "cuda")
+    dbg = {"seq_cap": SEQ}
+    _ops.trace_vorotracing_fwd(*args, None, 0.01, 1024, False, path=path, debug=dbg)
+    seq = dbg["seq"].cpu().numpy().reshape(nr, SEQ)
+    seq_len = dbg["seq_len"].cpu().numpy().reshape(-1)
+    cells = path.cells.cpu().numpy()
+    plen = path.len.cpu().numpy()
+    ref = oracle.trace_fwd(S, rays, start, wt=0.01, seq_cap=SEQ)
+    # the walk ends on a cell with no exit face, or stops integrating inside one
+    assert np.all((plen == seq_len) | (plen == seq_len - 1))
+    for r in range(nr):
+        # the exit neighbour of the last step is recorded but never entered
+        m = min(int(plen[r]), cap, int(seq_len[r]) - 1, SEQ - 1)
+        np.testing.assert_array_equal(cells[:m, r], seq[r, 1:m + 1])
+    assert np.array_equal(seq_len, np.asarray(ref["seq_len"]).reshape(-1))

@@ -20,6 +20,10 @@ class VtScene(C.Structure):
                 ("num_face_rows", C.c_uint64)]
 
 
+class VtPath(C.Structure):
+    _fields_ = [("cells", C.c_void_p), ("cap", C.c_uint32), ("len", C.c_void_p)]
+
+
 class VtDebug(C.Structure):
     _fields_ = [("seq", C.c_void_p), ("seq_cap", C.c_uint32), ("seq_len", C.c_void_p),
                 ("stats", C.c_void_p), ("num_intersections", C.c_void_p),

@@ -42,6 +42,7 @@ template <class AT> struct FwdOut {
     AT *contrib;
     float *dist, *W, *S, *tfar;
     WalkDebug dbg;
+    PathRec rec;
 };
 
 template <class AT, int R, bool kDebug>
@@ -57,11 +58,16 @@ __global__ void __launch_bounds__(kTrainBlock, VT_FWD_MIN_BLOCKS)
     uint32_t *qi = o.qidx ? o.qidx + (size_t)r * a.K : nullptr;
     FwdInteg<AT, R> I(ray, tex, a.wt, qthr, a.dq ? a.K : 0, qd, qi, o.contrib);
     uint32_t n = 0;
-    if (start < a.n_points)
+    if (start >= a.n_points) {
+        report(a.err, VT_ERR_DATA);
+        if (o.rec.cells) o.rec.len[r] = 0;
+    } else if (o.rec.cells) {
+        n = walk<FwdInteg<AT, R>, kDebug, true>(ray, a.faces, a.offs, a.points, a.density, start,
+                                                a.max_steps, I, r, o.dbg, o.rec);
+    } else {
         n = walk<FwdInteg<AT, R>, kDebug>(ray, a.faces, a.offs, a.points, a.density, start,
                                           a.max_steps, I, r, o.dbg);
-    else
-        report(a.err, VT_ERR_DATA);
+    }
     for (uint32_t i = I.qi; i < a.K; ++i) {
         qd[i] = -1.0f;
         qi[i] = 0xffffffffu;
@@ -91,6 +97,7 @@ template <class AT> struct BwdIn {
     float *density_grad;
     AT *point_error;
     float4 *sdiff, *sspec, *spts;  // padded scratch or null
+    PathRec rec;                   // forward's path record or null cells
 };
 
 template <class AT, int R, int F>
@@ -156,9 +163,14 @@ __global__ void __launch_bounds__(kTrainBlock, VT_BWD_MIN_BLOCKS)
     float tu, tv;
     oct_encode<R>(mk(-ray.d.x, -ray.d.y, -ray.d.z), tu, tv);
     I.spec = make_bilin<R>(tu, tv);
-    WalkDebug none{nullptr, 0, nullptr, nullptr, nullptr, nullptr};
-    walk<BwdInteg<AT, R, F>, false>(ray, a.faces, a.offs, a.points, a.density, start, a.max_steps, I,
-                                 r, none);
+    if (b.rec.cells) {
+        walk_replay<BwdInteg<AT, R, F>>(ray, a.faces, a.offs, a.points, a.density, start,
+                                        a.max_steps, I, r, b.rec);
+    } else {
+        WalkDebug none{nullptr, 0, nullptr, nullptr, nullptr, nullptr};
+        walk<BwdInteg<AT, R, F>, false>(ray, a.faces, a.offs, a.points, a.density, start,
+                                        a.max_steps, I, r, none);
+    }
 }
 
 // out[t*3 + c] += scratch[t].c for every texel (or site) t.
@@ -252,7 +264,8 @@ extern "C" vt_status vt_trace_fwd(const vt_scene *scene, int attr_half, const vo
                                   float *quantile_depths, uint32_t *quantile_indices,
                                   uint32_t *num_intersections, void *contribution,
                                   float *distortion, float *W_total, float *S_total, float *t_far,
-                                  const vt_debug *debug, uint32_t *err, vt_stream stream)
+                                  const vt_debug *debug, const vt_path *path, uint32_t *err,
+                                  vt_stream stream)
 {
     vt::TrainCommon a;
     vt_status st = vt::fill_common(a, scene, rays, num_rays, start, num_quantiles, depth_quantiles,
@@ -268,15 +281,20 @@ extern "C" vt_status vt_trace_fwd(const vt_scene *scene, int attr_half, const vo
     if (debug)
         dbg = vt::WalkDebug{debug->seq, debug->seq_cap, debug->seq_len, (uint4 *)debug->stats,
                             debug->visited, debug->textured};
+    vt::PathRec rec{nullptr, 0, 0, nullptr};
+    if (path && path->cells && path->cap) {
+        VT_REQUIRE(path->len, "vt_trace_fwd: path record without len");
+        rec = vt::PathRec{path->cells, path->cap, num_rays, path->len};
+    }
     cudaStream_t s = (cudaStream_t)stream;
     if (attr_half) {
         vt::FwdOut<__half> o{(__half *)rgba, quantile_depths, quantile_indices, num_intersections,
-                             (__half *)contribution, distortion, W_total, S_total, t_far, dbg};
+                             (__half *)contribution, distortion, W_total, S_total, t_far, dbg, rec};
         if (res == 8) return vt::launch_fwd<__half, 8>(a, diffuse, specular, o, debug, s);
         if (res == 4) return vt::launch_fwd<__half, 4>(a, diffuse, specular, o, debug, s);
     } else {
         vt::FwdOut<float> o{(float *)rgba, quantile_depths, quantile_indices, num_intersections,
-                            (float *)contribution, distortion, W_total, S_total, t_far, dbg};
+                            (float *)contribution, distortion, W_total, S_total, t_far, dbg, rec};
         if (res == 8) return vt::launch_fwd<float, 8>(a, diffuse, specular, o, debug, s);
         if (res == 4) return vt::launch_fwd<float, 4>(a, diffuse, specular, o, debug, s);
     }
@@ -301,7 +319,8 @@ extern "C" vt_status vt_trace_bwd(const vt_scene *scene, int attr_half, const vo
                                   float weight_threshold, uint32_t max_intersections,
                                   float *points_grad, void *diffuse_grad, void *specular_grad,
                                   float *density_grad, void *point_error, void *workspace,
-                                  uint64_t workspace_bytes, uint32_t *err, vt_stream stream)
+                                  uint64_t workspace_bytes, const vt_path *path, uint32_t *err,
+                                  vt_stream stream)
 {
     vt::TrainCommon a;
     vt_status st = vt::fill_common(a, scene, rays, num_rays, start, num_quantiles, depth_quantiles,
@@ -319,6 +338,11 @@ extern "C" vt_status vt_trace_bwd(const vt_scene *scene, int attr_half, const vo
     VT_REQUIRE(num_quantiles == 0 || (quantile_indices && depth_grad),
                "vt_trace_bwd: depth_grad must be provided if depth_quantiles is provided");
     if (num_rays == 0) return VT_OK;
+    vt::PathRec rec{nullptr, 0, 0, nullptr};
+    if (path && path->cells && path->cap) {
+        VT_REQUIRE(path->len, "vt_trace_bwd: path record without len");
+        rec = vt::PathRec{path->cells, path->cap, num_rays, path->len};
+    }
     cudaStream_t s = (cudaStream_t)stream;
     if (attr_half) {
         vt::BwdIn<__half> b{quantile_indices, (const __half *)rgba, (const __half *)rgba_grad,
@@ -326,6 +350,7 @@ extern "C" vt_status vt_trace_bwd(const vt_scene *scene, int attr_half, const vo
                             distortion, distortion_grad, W_total, S_total, points_grad,
                             (__half *)diffuse_grad, (__half *)specular_grad, density_grad,
                             (__half *)point_error};
+        b.rec = rec;
         if (res == 8) return vt::launch_bwd<__half, 8>(a, diffuse, specular, b, workspace, s);
         if (res == 4) return vt::launch_bwd<__half, 4>(a, diffuse, specular, b, workspace, s);
     } else {
@@ -334,6 +359,7 @@ extern "C" vt_status vt_trace_bwd(const vt_scene *scene, int attr_half, const vo
                            distortion, distortion_grad, W_total, S_total, points_grad,
                            (float *)diffuse_grad, (float *)specular_grad, density_grad,
                            (float *)point_error};
+        b.rec = rec;
         if (res == 8) return vt::launch_bwd<float, 8>(a, diffuse, specular, b, workspace, s);
         if (res == 4) return vt::launch_bwd<float, 4>(a, diffuse, specular, b, workspace, s);
     }

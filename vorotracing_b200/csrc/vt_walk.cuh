@@ -75,28 +75,56 @@ __device__ __forceinline__ void test_chunk_idx(const FaceChunk &c, uint32_t j, u
     }
 }
 
+// Path record of the training forward, replayed by the backward.  Slot k of
+// ray r holds the cell entered at walk step k (the exit neighbour found at
+// step k), laid out slot-major (cells[k * stride + r]) so that the lanes of a
+// warp, which advance one cell per loop iteration together, touch
+// consecutive words.  len[r] = number of exit faces found (steps past cap are
+// not stored; the replay then resumes the face scan where the record ends).
+struct PathRec {
+    uint32_t *cells;
+    uint32_t cap;
+    uint64_t stride;
+    uint32_t *len;
+};
+
+// Exit distance through the bisector face shared with site Q.  The packed
+// face row of that face holds off = binary16(Q - P) (pack_faces_kernel), so
+// this is test_chunk_idx's arithmetic on the same operands, bit for bit.
+__device__ __forceinline__ float face_exit_t(V3 P, V3 Q, const Ray &ray)
+{
+    const V3 d = Q - P;
+    const V3 off = mk(h2f(f2h(d.x)), h2f(f2h(d.y)), h2f(f2h(d.z)));
+    const V3 fo = fma3(off, 0.5f, P);
+    return dot(fo - ray.o, off) / dot(off, ray.d);
+}
+
+// Walk state: the cell being entered and everything the next step needs.
+struct WalkState {
+    uint32_t cur, begin, deg, n;
+    V3 P;
+    float s, t0;
+};
+
 // Integ must provide: bool integrate(uint32_t cell, float t0, float t1,
 //                                    V3 P, V3 Q, float density) and
 //                     uint32_t textured() const.
-template <class Integ, bool kDebug>
-__device__ __forceinline__ uint32_t walk(const Ray &ray, const uint4 *__restrict__ faces,
-                                         const uint32_t *__restrict__ offs,
-                                         const float *__restrict__ points,
-                                         const float *__restrict__ density, uint32_t start,
-                                         uint32_t max_steps, Integ &I, uint32_t ray_id,
-                                         const WalkDebug &dbg)
+// Runs the walk from state w; returns the step count n.
+template <class Integ, bool kDebug, bool kRecord>
+__device__ __forceinline__ uint32_t walk_from(WalkState w, const Ray &ray,
+                                              const uint4 *__restrict__ faces,
+                                              const float *__restrict__ points,
+                                              const float *__restrict__ density,
+                                              uint32_t max_steps, Integ &I, uint32_t ray_id,
+                                              const WalkDebug &dbg, const PathRec &rec)
 {
-    uint32_t cur = start;
-    uint32_t begin = __ldg(offs + cur);
-    uint32_t deg = __ldg(offs + cur + 1) - begin;
-    V3 P = ld3(points + (size_t)cur * 3);
-    float s = __ldg(density + cur);
+    uint32_t cur = w.cur, begin = w.begin, deg = w.deg, n = w.n;
+    V3 P = w.P;
+    float s = w.s, t0 = w.t0;
     FaceChunk c;
     load_chunk(c, faces + begin, 0, deg);
 
-    float t0 = 0.0f;
-    uint32_t n = 0;
-    uint32_t ns = 0, nfaces = 0, nint = 0;
+    uint32_t ns = 0, nfaces = 0, nint = 0, nfound = 0;
     for (;;) {
         n++;
         if (n > max_steps) break;
@@ -131,6 +159,10 @@ __device__ __forceinline__ uint32_t walk(const Ray &ray, const uint4 *__restrict
         }
 
         if (!x.found) break;
+        if (kRecord) {
+            if (nfound < rec.cap) rec.cells[(uint64_t)nfound * rec.stride + ray_id] = x.nb;
+            nfound++;
+        }
         // Issue the next cell's loads before integrating this one.
         V3 Q = ld3(points + (size_t)x.nb * 3);
         float sn = __ldg(density + x.nb);
@@ -153,7 +185,93 @@ __device__ __forceinline__ uint32_t walk(const Ray &ray, const uint4 *__restrict
         if (dbg.seq_len) dbg.seq_len[ray_id] = ns;
         if (dbg.stats) dbg.stats[ray_id] = make_uint4(ns, nfaces, nint, I.textured());
     }
+    if (kRecord && rec.len) rec.len[ray_id] = nfound;
     return n;
+}
+
+template <class Integ, bool kDebug, bool kRecord = false>
+__device__ __forceinline__ uint32_t walk(const Ray &ray, const uint4 *__restrict__ faces,
+                                         const uint32_t *__restrict__ offs,
+                                         const float *__restrict__ points,
+                                         const float *__restrict__ density, uint32_t start,
+                                         uint32_t max_steps, Integ &I, uint32_t ray_id,
+                                         const WalkDebug &dbg,
+                                         const PathRec &rec = PathRec{nullptr, 0, 0, nullptr})
+{
+    WalkState w;
+    w.cur = start;
+    w.begin = __ldg(offs + start);
+    w.deg = __ldg(offs + start + 1) - w.begin;
+    w.P = ld3(points + (size_t)start * 3);
+    w.s = __ldg(density + start);
+    w.t0 = 0.0f;
+    w.n = 0;
+    return walk_from<Integ, kDebug, kRecord>(w, ray, faces, points, density, max_steps, I, ray_id,
+                                             dbg, rec);
+}
+
+// Backward replay: the cells of the forward's path record are entered
+// without scanning faces (the exit distance is recomputed from the two
+// sites), then the ordinary walk resumes where the record ends.  The walk is
+// deterministic, so every recorded step is the step the scan would take.
+// The record of step k+1 and the site of step k+1 are loaded one iteration
+// ahead.
+template <class Integ>
+__device__ __forceinline__ void walk_replay(const Ray &ray, const uint4 *__restrict__ faces,
+                                            const uint32_t *__restrict__ offs,
+                                            const float *__restrict__ points,
+                                            const float *__restrict__ density, uint32_t start,
+                                            uint32_t max_steps, Integ &I, uint32_t ray_id,
+                                            const PathRec &rec)
+{
+    const uint32_t L = min(min(__ldg(rec.len + ray_id), rec.cap), max_steps);
+    const uint32_t *cells = rec.cells + ray_id;
+    uint32_t cur = start;
+    V3 P = ld3(points + (size_t)start * 3);
+    float s = __ldg(density + start);
+    float t0 = 0.0f;
+    uint32_t k = 0;
+    uint32_t nb = 0, nb1 = 0;
+    V3 Q = P;
+    float sq = 0.0f;
+    if (L > 0) {
+        nb = __ldg(cells);
+        Q = ld3(points + (size_t)nb * 3);
+        sq = __ldg(density + nb);
+    }
+    if (L > 1) nb1 = __ldg(cells + rec.stride);
+    for (; k < L; ++k) {
+        // prefetch step k+1's site and step k+2's record
+        V3 Qn = Q;
+        float sqn = 0.0f;
+        uint32_t nb2 = 0;
+        if (k + 1 < L) {
+            Qn = ld3(points + (size_t)nb1 * 3);
+            sqn = __ldg(density + nb1);
+        }
+        if (k + 2 < L) nb2 = __ldg(cells + (uint64_t)(k + 2) * rec.stride);
+        const float t1 = face_exit_t(P, Q, ray);
+        if (t1 > t0 && !I.integrate(cur, t0, t1, P, Q, s)) return;
+        t0 = fmaxf(t0, t1);
+        cur = nb;
+        P = Q;
+        s = sq;
+        nb = nb1;
+        Q = Qn;
+        sq = sqn;
+        nb1 = nb2;
+    }
+    WalkState w;
+    w.cur = cur;
+    w.begin = __ldg(offs + cur);
+    w.deg = __ldg(offs + cur + 1) - w.begin;
+    w.P = P;
+    w.s = s;
+    w.t0 = t0;
+    w.n = L;
+    WalkDebug none{nullptr, 0, nullptr, nullptr, nullptr, nullptr};
+    walk_from<Integ, false, false>(w, ray, faces, points, density, max_steps, I, ray_id, none,
+                                   PathRec{nullptr, 0, 0, nullptr});
 }
 
 }  // namespace vt

@@ -437,14 +437,38 @@ def _train_checks(points, diffuse, specular, density, adjacency, offsets, rays, 
     return nr
 
 
+class PathRecord:
+    """Per-ray cell sequence written by the training forward and replayed by
+    the backward (vt_path): ``cells`` (cap, num_rays) uint32 slot-major,
+    ``len`` (num_rays,) uint32.  cap * num_rays * 4 bytes of device memory;
+    rays longer than ``cap`` steps resume the face scan after the stored
+    prefix."""
+
+    def __init__(self, num_rays: int, cap: int, device):
+        self.cap = int(cap)
+        self.num_rays = int(num_rays)
+        self.cells = torch.empty((self.cap, self.num_rays), dtype=torch.uint32, device=device)
+        self.len = torch.empty(self.num_rays, dtype=torch.uint32, device=device)
+
+    def struct(self, nr: int):
+        if nr != self.num_rays:
+            _fail("path record was made for a different number of rays")
+        return _lib.VtPath(self.cells.data_ptr(), self.cap, self.len.data_ptr())
+
+
+def _path_arg(path, nr):
+    return None if path is None else C.byref(path.struct(nr))
+
+
 def trace_vorotracing_fwd(points, diffuse, specular, density, adjacency, offsets, rays,
                           start_point, depth_quantiles, weight_threshold: float,
                           max_intersections: int, return_contribution: bool, faces=None,
-                          debug: dict | None = None):
+                          debug: dict | None = None, path: PathRecord | None = None):
     """Training forward (tracing_octmap.cu:355-546).  Returns the reference's
     9-tuple (rgba, depth, depth_indices, contribution, num_intersections,
     distortion, W_total, S_total, t_far); depth / depth_indices /
-    contribution are None when not requested."""
+    contribution are None when not requested.  ``path``: a PathRecord to
+    fill for the backward."""
     points, diffuse, specular = points.contiguous(), diffuse.contiguous(), specular.contiguous()
     density, adjacency, offsets = density.contiguous(), adjacency.contiguous(), offsets.contiguous()
     rays, start_point = _aligned(rays, 8), start_point.contiguous()
@@ -486,7 +510,7 @@ def trace_vorotracing_fwd(points, diffuse, specular, density, adjacency, offsets
                              C.c_uint32(K), ptr(dq), C.c_float(weight_threshold),
                              C.c_uint32(max_intersections), ptr(rgba), ptr(depth), ptr(depth_idx),
                              ptr(n_int), ptr(contrib), ptr(dist), ptr(W), ptr(S), ptr(tfar), dbg,
-                             ptr(err), stream_ptr(dev)), "vt_trace_fwd")
+                             _path_arg(path, nr), ptr(err), stream_ptr(dev)), "vt_trace_fwd")
     if debug is not None or _CHECK_ERRORS:
         _check_err(err)
     del keep
@@ -498,12 +522,14 @@ def trace_vorotracing_bwd(points, diffuse, specular, density, adjacency, offsets
                           depth_grad, ray_error, contribution_alpha_grad: float, distortion,
                           distortion_grad, W_total, S_total, t_far, weight_threshold: float,
                           max_intersections: int, faces=None, grads=None,
-                          vector_atomics: bool = True):
+                          vector_atomics: bool = True, path: PathRecord | None = None):
     """Training backward (tracing_octmap.cu:860-1103).  Gradients go to new
     zeroed tensors, or accumulate into ``grads`` = (points, diffuse, specular,
     density) when given.  Returns the reference's 6-tuple (points_grad, diffuse_grad, specular_grad, density_grad, ray_grad,
     point_error); ray_grad is allocated and never written, as in the
-    reference; point_error is None unless ray_error is given."""
+    reference; point_error is None unless ray_error is given.  ``path``: the
+    PathRecord filled by the forward of the same inputs (the walk then skips
+    the face scan of the recorded steps; results are unchanged)."""
     points, diffuse, specular = points.contiguous(), diffuse.contiguous(), specular.contiguous()
     density, adjacency, offsets = density.contiguous(), adjacency.contiguous(), offsets.contiguous()
     rays, start_point = _aligned(rays, 8), start_point.contiguous()
@@ -602,7 +628,8 @@ def trace_vorotracing_bwd(points, diffuse, specular, density, adjacency, offsets
                              ptr(ts["S_total"]), C.c_float(weight_threshold),
                              C.c_uint32(max_intersections), ptr(points_grad), ptr(diffuse_grad),
                              ptr(specular_grad), ptr(density_grad), ptr(perr), ptr(ws),
-                             C.c_uint64(wsb), ptr(err), stream_ptr(dev)), "vt_trace_bwd")
+                             C.c_uint64(wsb), _path_arg(path, nr), ptr(err), stream_ptr(dev)),
+          "vt_trace_bwd")
     if _CHECK_ERRORS:
         _check_err(err)
     return points_grad, diffuse_grad, specular_grad, density_grad, ray_grad, perr

@@ -26,18 +26,28 @@ class TraceVoroTracing(torch.autograd.Function):
     return_contribution) -> (rgba, depth, contribution, num_intersections,
     errbox, distortion).  Gradients flow to the first four inputs.  The packed
     face rows built in forward are reused by backward (the sites cannot change
-    in between), where the reference rebuilds its adj_diff on every call."""
+    in between), where the reference rebuilds its adj_diff on every call.
+
+    The forward also records each ray's first ``path_cap`` cells
+    (``path_cap`` * 4 bytes per ray, held until backward) so that the
+    backward enters them without scanning faces; set ``path_cap = 0`` to
+    re-walk instead.  Gradients are the same either way."""
+
+    path_cap = 256
 
     @staticmethod
     def forward(ctx, _points, _diffuse, _specular, _density, _point_adjacency,
                 _point_adjacency_offsets, rays, start_point, depth_quantiles,
                 weight_threshold: float, max_intersections: int, return_contribution: bool):
         faces = _ops.prefetch_faces(_points, _point_adjacency, _point_adjacency_offsets)
+        cap = min(int(TraceVoroTracing.path_cap), int(max_intersections))
+        path = _ops.PathRecord(rays.numel() // 6, cap, rays.device) if cap > 0 else None
         (rgba, depth, depth_indices, contribution, num_intersections, distortion, W_total,
          S_total, t_far) = _ops.trace_vorotracing_fwd(
             _points, _diffuse, _specular, _density, _point_adjacency, _point_adjacency_offsets,
             rays, start_point, depth_quantiles, weight_threshold, max_intersections,
-            return_contribution, faces=faces)
+            return_contribution, faces=faces, path=path)
+        ctx.path = path
         ctx.args = (_points, _diffuse, _specular, _density, _point_adjacency,
                     _point_adjacency_offsets, rays, start_point)
         ctx.depth_quantiles = depth_quantiles
@@ -65,7 +75,7 @@ class TraceVoroTracing(torch.autograd.Function):
                 *ctx.args, ctx.rgba, g_rgba, ctx.depth_quantiles, ctx.depth_indices,
                 g_depth if ctx.depth_quantiles is not None else None, ray_error, contrib,
                 ctx.distortion, g_dist, ctx.W_total, ctx.S_total, ctx.t_far,
-                ctx.weight_threshold, ctx.max_intersections, faces=ctx.faces)
+                ctx.weight_threshold, ctx.max_intersections, faces=ctx.faces, path=ctx.path)
 
         if ctx.depth_quantiles is not None and grad_depth is None:
             grad_depth = torch.zeros(ctx.depth_indices.shape, dtype=torch.float32,
@@ -88,7 +98,7 @@ class TraceVoroTracing(torch.autograd.Function):
         ctx.errbox.point_error = point_error
         for t in (points_grad, diffuse_grad, specular_grad, density_grad):
             torch.nan_to_num(t, nan=0.0, posinf=0.0, neginf=0.0, out=t)
-        del ctx.args, ctx.faces, ctx.rgba, ctx.distortion, ctx.W_total, ctx.S_total, ctx.t_far
+        del ctx.args, ctx.faces, ctx.path, ctx.rgba, ctx.distortion, ctx.W_total, ctx.S_total, ctx.t_far
         return (points_grad, diffuse_grad, specular_grad, density_grad, None, None, None, None,
                 None, None, None, None)
 
