@@ -135,10 +135,13 @@ VT_API vt_status vt_trace_depth(const vt_scene *scene, const float *rays, uint32
 /* Path record: the training forward stores, for each ray, the cell it enters
  * at every walk step (cells (cap, num_rays) u32, slot-major: cells[k *
  * num_rays + r]) and the number of steps that found an exit face (len
- * (num_rays) u32; steps beyond cap are not stored).  Given the same record,
- * the backward enters the recorded cells without scanning their faces and
- * resumes the face scan after the last stored step, with results identical
- * to a backward without the record.  The record is only valid for the scene,
+ * (num_rays) u32; steps beyond cap are not stored).  Bit 31 of len flags a
+ * ray that the backward must walk itself: the record overflowed, or the
+ * forward stopped at T == weight_threshold exactly (the backward's stop rule
+ * is T < weight_threshold).  Given the same record, the backward enters the
+ * recorded cells of the other rays without scanning their faces, and walks
+ * the flagged ones in a second launch, with results identical to a backward
+ * without the record.  The record is only valid for the scene,
  * rays, start cells and max_intersections of the forward that wrote it.  No
  * reference counterpart (the reference's backward re-walks every ray). */
 typedef struct {

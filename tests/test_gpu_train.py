@@ -245,7 +245,10 @@ def test_path_record_is_the_cell_sequence(c1_scene, c1_rays, cap):
     seq = dbg["seq"].cpu().numpy().reshape(nr, SEQ)
     seq_len = dbg["seq_len"].cpu().numpy().reshape(-1)
     cells = path.cells.cpu().numpy()
-    plen = path.len.cpu().numpy()
+    plen_raw = path.len.cpu().numpy()
+    plen = plen_raw & 0x7FFFFFFF
+    # the high bit asks the backward to walk the ray itself (record overflow)
+    assert np.all(((plen_raw >> 31) == 1) >= (plen > cap))
     ref = oracle.trace_fwd(S, rays, start, wt=0.01, seq_cap=SEQ)
     # the walk ends on a cell with no exit face, or stops integrating inside one
     assert np.all((plen == seq_len) | (plen == seq_len - 1))

@@ -60,7 +60,7 @@ __global__ void __launch_bounds__(kTrainBlock, VT_FWD_MIN_BLOCKS)
     uint32_t n = 0;
     if (start >= a.n_points) {
         report(a.err, VT_ERR_DATA);
-        if (o.rec.cells) o.rec.len[r] = 0;
+        if (o.rec.cells) o.rec.len[r] = kPathWalk;
     } else if (o.rec.cells) {
         n = walk<FwdInteg<AT, R>, kDebug, true>(ray, a.faces, a.offs, a.points, a.density, start,
                                                 a.max_steps, I, r, o.dbg, o.rec);
@@ -68,6 +68,7 @@ __global__ void __launch_bounds__(kTrainBlock, VT_FWD_MIN_BLOCKS)
         n = walk<FwdInteg<AT, R>, kDebug>(ray, a.faces, a.offs, a.points, a.density, start,
                                           a.max_steps, I, r, o.dbg);
     }
+    if (o.rec.cells && (o.rec.len[r] > o.rec.cap || I.T == a.wt)) o.rec.len[r] |= kPathWalk;
     for (uint32_t i = I.qi; i < a.K; ++i) {
         qd[i] = -1.0f;
         qi[i] = 0xffffffffu;
@@ -100,12 +101,21 @@ template <class AT> struct BwdIn {
     PathRec rec;                   // forward's path record or null cells
 };
 
-template <class AT, int R, int F>
+// Backward launch modes: walk every ray; replay the rays of a path record;
+// walk only the rays the record flags.
+constexpr int kBwdWalkAll = 0, kBwdReplay = 1, kBwdWalkFlagged = 2;
+
+template <class AT, int R, int F, int M>
 __global__ void __launch_bounds__(kTrainBlock, VT_BWD_MIN_BLOCKS)
     bwd_kernel(TrainCommon a, TexPlain<AT, R> tex, BwdIn<AT> b)
 {
     uint32_t r = blockIdx.x * blockDim.x + threadIdx.x;
     if (r >= a.num_rays) return;
+    uint32_t L = 0;
+    if (M != kBwdWalkAll) {
+        L = __ldg(b.rec.len + r);
+        if ((M == kBwdReplay) == ((L & kPathWalk) != 0)) return;
+    }
     Ray ray = load_ray(a.rays, r);
     uint32_t start = __ldg(a.start + r);
     if (start >= a.n_points) {
@@ -163,9 +173,9 @@ __global__ void __launch_bounds__(kTrainBlock, VT_BWD_MIN_BLOCKS)
     float tu, tv;
     oct_encode<R>(mk(-ray.d.x, -ray.d.y, -ray.d.z), tu, tv);
     I.spec = make_bilin<R>(tu, tv);
-    if (b.rec.cells) {
-        walk_replay<BwdInteg<AT, R, F>>(ray, a.faces, a.offs, a.points, a.density, start,
-                                        a.max_steps, I, r, b.rec);
+    if (M == kBwdReplay) {
+        walk_replay<BwdInteg<AT, R, F>>(ray, a.points, a.density, start, min(L, a.max_steps), I,
+                                        b.rec.cells + r, b.rec.stride);
     } else {
         WalkDebug none{nullptr, 0, nullptr, nullptr, nullptr, nullptr};
         walk<BwdInteg<AT, R, F>, false>(ray, a.faces, a.offs, a.points, a.density, start,
@@ -239,7 +249,12 @@ vt_status launch_bwd(const TrainCommon &a, const void *dif, const void *spe, Bwd
     switch (F) {
 #define VT_BWD_CASE(f)                                                                             \
     case f:                                                                                        \
-        bwd_kernel<AT, R, f><<<g, kTrainBlock, 0, s>>>(a, t, b);                                   \
+        if (b.rec.cells) {                                                                         \
+            bwd_kernel<AT, R, f, kBwdReplay><<<g, kTrainBlock, 0, s>>>(a, t, b);                   \
+            bwd_kernel<AT, R, f, kBwdWalkFlagged><<<g, kTrainBlock, 0, s>>>(a, t, b);              \
+        } else {                                                                                   \
+            bwd_kernel<AT, R, f, kBwdWalkAll><<<g, kTrainBlock, 0, s>>>(a, t, b);                  \
+        }                                                                                          \
         break;
         VT_BWD_CASE(0) VT_BWD_CASE(1) VT_BWD_CASE(2) VT_BWD_CASE(3)
         VT_BWD_CASE(4) VT_BWD_CASE(5) VT_BWD_CASE(6) VT_BWD_CASE(7)

@@ -210,27 +210,29 @@ __device__ __forceinline__ uint32_t walk(const Ray &ray, const uint4 *__restrict
                                              dbg, rec);
 }
 
+// Flag in PathRec::len: the backward must walk this ray itself (the record
+// overflowed, or the forward stopped at T == weight_threshold exactly, where
+// the backward's stop rule T < weight_threshold lets the walk go on).
+constexpr uint32_t kPathWalk = 0x80000000u;
+
 // Backward replay: the cells of the forward's path record are entered
 // without scanning faces (the exit distance is recomputed from the two
-// sites), then the ordinary walk resumes where the record ends.  The walk is
-// deterministic, so every recorded step is the step the scan would take.
-// The record of step k+1 and the site of step k+1 are loaded one iteration
-// ahead.
+// sites).  The walk is deterministic, so every recorded step is the step the
+// scan would take, and an unflagged record ends where the backward's walk
+// ends (no exit face, the step limit, or T < weight_threshold, which stopped
+// the forward at the same step).  Flagged rays are skipped here and walked
+// by a second launch.  The record of step k+2 and the site of step k+1 are
+// loaded one iteration ahead.
 template <class Integ>
-__device__ __forceinline__ void walk_replay(const Ray &ray, const uint4 *__restrict__ faces,
-                                            const uint32_t *__restrict__ offs,
-                                            const float *__restrict__ points,
+__device__ __forceinline__ void walk_replay(const Ray &ray, const float *__restrict__ points,
                                             const float *__restrict__ density, uint32_t start,
-                                            uint32_t max_steps, Integ &I, uint32_t ray_id,
-                                            const PathRec &rec)
+                                            uint32_t L, Integ &I, const uint32_t *cells,
+                                            uint64_t stride)
 {
-    const uint32_t L = min(min(__ldg(rec.len + ray_id), rec.cap), max_steps);
-    const uint32_t *cells = rec.cells + ray_id;
     uint32_t cur = start;
     V3 P = ld3(points + (size_t)start * 3);
     float s = __ldg(density + start);
     float t0 = 0.0f;
-    uint32_t k = 0;
     uint32_t nb = 0, nb1 = 0;
     V3 Q = P;
     float sq = 0.0f;
@@ -239,9 +241,8 @@ __device__ __forceinline__ void walk_replay(const Ray &ray, const uint4 *__restr
         Q = ld3(points + (size_t)nb * 3);
         sq = __ldg(density + nb);
     }
-    if (L > 1) nb1 = __ldg(cells + rec.stride);
-    for (; k < L; ++k) {
-        // prefetch step k+1's site and step k+2's record
+    if (L > 1) nb1 = __ldg(cells + stride);
+    for (uint32_t k = 0; k < L; ++k) {
         V3 Qn = Q;
         float sqn = 0.0f;
         uint32_t nb2 = 0;
@@ -249,7 +250,7 @@ __device__ __forceinline__ void walk_replay(const Ray &ray, const uint4 *__restr
             Qn = ld3(points + (size_t)nb1 * 3);
             sqn = __ldg(density + nb1);
         }
-        if (k + 2 < L) nb2 = __ldg(cells + (uint64_t)(k + 2) * rec.stride);
+        if (k + 2 < L) nb2 = __ldg(cells + (uint64_t)(k + 2) * stride);
         const float t1 = face_exit_t(P, Q, ray);
         if (t1 > t0 && !I.integrate(cur, t0, t1, P, Q, s)) return;
         t0 = fmaxf(t0, t1);
@@ -261,17 +262,6 @@ __device__ __forceinline__ void walk_replay(const Ray &ray, const uint4 *__restr
         sq = sqn;
         nb1 = nb2;
     }
-    WalkState w;
-    w.cur = cur;
-    w.begin = __ldg(offs + cur);
-    w.deg = __ldg(offs + cur + 1) - w.begin;
-    w.P = P;
-    w.s = s;
-    w.t0 = t0;
-    w.n = L;
-    WalkDebug none{nullptr, 0, nullptr, nullptr, nullptr, nullptr};
-    walk_from<Integ, false, false>(w, ray, faces, points, density, max_steps, I, ray_id, none,
-                                   PathRec{nullptr, 0, 0, nullptr});
 }
 
 }  // namespace vt
