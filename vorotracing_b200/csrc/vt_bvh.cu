@@ -21,20 +21,11 @@
 #include <cub/device/device_radix_sort.cuh>
 
 #include "vt_abi.cuh"
-#include "vt_geom.cuh"
+#include "vt_bvh.cuh"
 
 namespace vt {
 namespace bvh {
 
-struct __align__(16) Node {
-    float lo[3];
-    uint32_t left;
-    float hi[3];
-    uint32_t right;
-};
-
-constexpr uint32_t kLeaf = 0x80000000u;
-constexpr int kStack = 96;
 
 __device__ __forceinline__ int f2ord(float f)
 {
@@ -173,15 +164,6 @@ __global__ void boxes_kernel(const float *__restrict__ p, int n, Node *nodes,
     }
 }
 
-__device__ __forceinline__ float box_d2(const Node &b, V3 q)
-{
-    float dx = fmaxf(fmaxf(b.lo[0] - q.x, 0.0f), q.x - b.hi[0]);
-    float dy = fmaxf(fmaxf(b.lo[1] - q.y, 0.0f), q.y - b.hi[1]);
-    float dz = fmaxf(fmaxf(b.lo[2] - q.z, 0.0f), q.z - b.hi[2]);
-    // same contracted form as the site distance dot(d, d), so the bound stays
-    // below the distance of every site in the box (RN and fma are monotone)
-    return dot(mk(dx, dy, dz), mk(dx, dy, dz));
-}
 
 __device__ __forceinline__ void visit_leaf(const float *__restrict__ p, uint32_t id, V3 q,
                                            float &best, uint32_t &bi)

@@ -30,7 +30,7 @@
 #include <cub/device/device_scan.cuh>
 
 #include "vt_abi.cuh"
-#include "vt_geom.cuh"
+#include "vt_bvh.cuh"
 
 namespace vt {
 namespace vor {
@@ -46,7 +46,7 @@ struct Cell {
     uint8_t tri[kMaxTris][3];      // plane ids
     uint8_t nbr[kMaxTris][3];      // triangle across edge (v0v1, v1v2, v2v0)
     float3 pos[kMaxTris];
-    bool alive[kMaxTris];
+    uint8_t alive[kMaxTris];       // 0 removed, 1 live, 2 live and verified (empty ball)
     int nplanes, ntris;
 };
 
@@ -83,7 +83,7 @@ __device__ void init_box(Cell &C, float B)
         float3 x;
         solve3(C.plane[T[t][0]], C.plane[T[t][1]], C.plane[T[t][2]], x);
         C.pos[t] = x;
-        C.alive[t] = true;
+        C.alive[t] = 1;
     }
     C.ntris = 8;
     // neighbours: the triangle sharing the reversed edge
@@ -121,8 +121,9 @@ __device__ void compact_planes(Cell &C)
     C.nplanes = k;
 }
 
-// Clip by plane (n, d).  Returns false on overflow / degeneracy (cell unusable).
-__device__ bool clip(Cell &C, float4 pl, uint32_t site)
+// Clip by plane (n, d).  Returns false on overflow / degeneracy (cell
+// unusable); *cut (if given) tells whether the plane removed any vertex.
+__device__ bool clip(Cell &C, float4 pl, uint32_t site, bool *cut = nullptr)
 {
     bool out[kMaxTris];
     int nout = 0, nin = 0;
@@ -137,6 +138,7 @@ __device__ bool clip(Cell &C, float4 pl, uint32_t site)
             ++nin;
         }
     }
+    if (cut) *cut = nout > 0;
     if (nout == 0) return true;  // plane misses the cell
     if (nin == 0) return false;  // everything cut: degenerate input
     if (C.nplanes >= kMaxPlanes) compact_planes(C);
@@ -160,7 +162,7 @@ __device__ bool clip(Cell &C, float4 pl, uint32_t site)
     }
     if (ne < 3) return false;
     for (int t = 0; t < C.ntris; ++t)
-        if (out[t]) C.alive[t] = false;
+        if (out[t]) C.alive[t] = 0;
     C.plane[np] = pl;
     C.site[np] = site;
     int8_t start_of[kMaxPlanes];
@@ -187,7 +189,7 @@ __device__ bool clip(Cell &C, float4 pl, uint32_t site)
         C.nbr[slot][1] = kNone;
         C.nbr[slot][2] = kNone;
         C.pos[slot] = x;
-        C.alive[slot] = true;
+        C.alive[slot] = 1;
         for (int m = 0; m < 3; ++m)
             if (C.tri[n][m] == b && C.tri[n][(m + 1) % 3] == a) C.nbr[n][m] = (uint8_t)slot;
         if (start_of[a] != -1) return false;  // boundary is not a simple cycle
@@ -280,6 +282,24 @@ __global__ void grid_scatter(uint32_t n, const uint32_t *cell_id, uint32_t *curs
     sorted[slot] = i;
 }
 
+// Sites of each grid cell in ascending id order (the scatter's atomic slots
+// are in arbitrary order), so that every scan order is reproducible.
+__global__ void grid_sort(uint32_t ncells, const uint32_t *__restrict__ start, uint32_t *sorted)
+{
+    const uint32_t c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= ncells) return;
+    const uint32_t b = start[c], e = start[c + 1];
+    for (uint32_t a = b + 1; a < e; ++a) {
+        const uint32_t v = sorted[a];
+        uint32_t k = a;
+        while (k > b && sorted[k - 1] > v) {
+            sorted[k] = sorted[k - 1];
+            --k;
+        }
+        sorted[k] = v;
+    }
+}
+
 // k nearest neighbours of site i (excluding i), ascending (distance, id).
 __device__ int knn(const float *__restrict__ p, uint32_t i, const Grid &g,
                    const uint32_t *__restrict__ start, const uint32_t *__restrict__ sorted, int k,
@@ -326,38 +346,120 @@ __device__ int knn(const float *__restrict__ p, uint32_t i, const Grid &g,
     return found;
 }
 
-constexpr int kKnnMax = 128;
+constexpr int kSeedK = 24;     // nearest sites clipped before verification
+constexpr int kMaxClips = 768;  // clips of one cell in verification (then the fallback)
 
-__global__ void __launch_bounds__(64) cell_kernel(const float *__restrict__ p, uint32_t n, Grid g,
-                                                  const uint32_t *__restrict__ start,
-                                                  const uint32_t *__restrict__ sorted, int k,
-                                                  float box, const uint32_t *__restrict__ todo,
-                                                  uint32_t ntodo, uint32_t *__restrict__ nbr_out,
-                                                  uint32_t stride, uint32_t *__restrict__ count,
-                                                  uint32_t *__restrict__ retry, uint32_t *nretry)
+// Clip the cell by a site that cuts its vertex v (coordinates relative to
+// site i at q): a site closer to v than site i, i.e. inside the ball
+// B(q + v, |v|).  The sites' BVH is traversed nearest child first, pruning
+// boxes farther than |v| (with a relative slack of 2^-10 covering the
+// rounding difference between absolute and site-relative coordinates); the
+// cut itself is decided by the clip's own plane test.  Sites skip0..2 (the
+// planes through v) are ignored.  Returns 1 if the cell was clipped, 0 if no
+// site cuts v, -1 if clipping failed.
+__device__ int bvh_cut(Cell &C, const float *__restrict__ p, uint32_t i, float3 q, float3 v,
+                       const bvh::Node *__restrict__ nodes, const uint32_t *__restrict__ ids,
+                       uint32_t skip0, uint32_t skip1, uint32_t skip2)
 {
-    uint32_t t = blockIdx.x * blockDim.x + threadIdx.x;
-    if (t >= ntodo) return;
-    uint32_t i = todo ? todo[t] : t;
-    float kd[kKnnMax];
-    uint32_t ki[kKnnMax];
-    int found = knn(p, i, g, start, sorted, k, kd, ki);
+    const V3 x = mk(q.x + v.x, q.y + v.y, q.z + v.z);
+    const float r2 = v.x * v.x + v.y * v.y + v.z * v.z;
+    const float lim = r2 + r2 * 0.0009765625f;
+    uint32_t stack[bvh::kStack];
+    int sp = 0;
+    uint32_t cur = 0;
+    for (;;) {
+        if (cur & bvh::kLeaf) {
+            const uint32_t j = __ldg(ids + (cur & ~bvh::kLeaf));
+            if (j != i && j != skip0 && j != skip1 && j != skip2) {
+                const float nx = p[3 * j] - q.x, ny = p[3 * j + 1] - q.y, nz = p[3 * j + 2] - q.z;
+                const float4 pl = make_float4(nx, ny, nz, 0.5f * (nx * nx + ny * ny + nz * nz));
+                if (pl.x * v.x + pl.y * v.y + pl.z * v.z - pl.w > 0.0f) {
+                    bool cut = false;
+                    if (!clip(C, pl, j, &cut)) return -1;
+                    if (cut) return 1;
+                }
+            }
+        } else {
+            const bvh::Node nd = nodes[cur];
+            const uint32_t c[2] = {nd.left, nd.right};
+            float dd[2];
+            for (int k = 0; k < 2; ++k) {
+                if (c[k] & bvh::kLeaf) {
+                    const V3 dv = x - ld3(p + (size_t)__ldg(ids + (c[k] & ~bvh::kLeaf)) * 3);
+                    dd[k] = dot(dv, dv);
+                } else {
+                    dd[k] = bvh::box_d2(nodes[c[k]], x);
+                }
+            }
+            const int nearf = dd[1] < dd[0] ? 1 : 0;
+            if (dd[1 - nearf] <= lim) {
+                if (sp >= bvh::kStack) return -1;
+                stack[sp++] = c[1 - nearf];
+            }
+            if (dd[nearf] <= lim) {
+                cur = c[nearf];
+                continue;
+            }
+        }
+        if (sp == 0) return 0;
+        cur = stack[--sp];
+    }
+}
+
+// One cell per thread: clip by the kSeedK nearest sites, then verify every
+// vertex v of the cell by the empty-ball property of Delaunay: no site may be
+// closer to v than site i.  A site found inside a vertex's ball clips the
+// cell (removing that vertex), and verification goes on over the new
+// vertices until every vertex's ball is empty; the cell is then exact (for a
+// convex-hull site: exact inside the truncation box).  The balls are searched
+// in the sites' BVH, so long needle-shaped cells along dense sheets and far
+// vertices of hull cells cost the nodes their balls touch.  Cells whose
+// clipping fails go to the retry list.
+__global__ void __launch_bounds__(64) cell_verify_kernel(
+    const float *__restrict__ p, uint32_t n, Grid g, const uint32_t *__restrict__ start,
+    const uint32_t *__restrict__ sorted, const bvh::Node *__restrict__ nodes,
+    const uint32_t *__restrict__ ids, float box, uint32_t *__restrict__ nbr_out, uint32_t stride,
+    uint32_t *__restrict__ count, uint32_t *__restrict__ retry, uint32_t *nretry)
+{
+    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    float kd[kSeedK];
+    uint32_t ki[kSeedK];
+    const int found = knn(p, i, g, start, sorted, kSeedK, kd, ki);
     Cell C;
     init_box(C, box);
-    float3 q = make_float3(p[3 * i], p[3 * i + 1], p[3 * i + 2]);
-    bool ok = true, secure = false;
+    const float3 q = make_float3(p[3 * i], p[3 * i + 1], p[3 * i + 2]);
+    bool ok = true;
     for (int m = 0; m < found && ok; ++m) {
-        if (kd[m] > 4.0f * max_vertex_r2(C)) {
-            secure = true;
-            break;
-        }
-        uint32_t j = ki[m];
-        float nx = p[3 * j] - q.x, ny = p[3 * j + 1] - q.y, nz = p[3 * j + 2] - q.z;
+        const uint32_t j = ki[m];
+        const float nx = p[3 * j] - q.x, ny = p[3 * j + 1] - q.y, nz = p[3 * j + 2] - q.z;
         ok = clip(C, make_float4(nx, ny, nz, 0.5f * (nx * nx + ny * ny + nz * nz)), j);
     }
-    if (ok && !secure && found < k) secure = true;  // every other site was considered
-    if (!ok || !secure) {
-        uint32_t r = atomicAdd(nretry, 1u);
+    int clips = 0;
+    int t = 0;
+    while (ok && t < C.ntris) {
+        if (C.alive[t] != 1) {
+            ++t;
+            continue;
+        }
+        const uint32_t s0 = C.site[C.tri[t][0]], s1 = C.site[C.tri[t][1]], s2 = C.site[C.tri[t][2]];
+        const int res = bvh_cut(C, p, i, q, C.pos[t], nodes, ids, s0, s1, s2);
+        if (res < 0 || ++clips > kMaxClips) {
+            ok = false;
+            break;
+        }
+        if (res == 0) {
+            C.alive[t] = 2;
+            ++t;
+        } else {
+            t = 0;  // new vertices may sit in reused slots
+        }
+    }
+    if (!ok) {
+#ifdef VT_VOR_VERBOSE
+        printf("verify failed: site %u clips %d ntris %d nplanes %d\n", i, clips, C.ntris, C.nplanes);
+#endif
+        const uint32_t r = atomicAdd(nretry, 1u);
         retry[r] = i;
         count[i] = 0;
         return;
@@ -437,6 +539,8 @@ struct VorWs {
     uint32_t *cnt, *start, *cell_id, *sorted, *count, *retry, *nretry, *nbr;
     void *temp;
     size_t temp_bytes;
+    void *bvh;       // the sites' BVH (vt_bvh_build blob)
+    void *bvh_ws;    // its build workspace
 };
 
 inline uint32_t grid_cells_bound(uint32_t n) { return 2 * n + 64; }
@@ -469,6 +573,9 @@ inline VorWs carve(void *ws, uint32_t n)
     v.nbr = (uint32_t *)w;      w += a256((size_t)n * kMaxPlanes * 4);
     v.temp = w;
     v.temp_bytes = scan_bytes(n);
+    w += a256(v.temp_bytes);
+    v.bvh = w;                  w += a256(vt_bvh_nodes_bytes(n));
+    v.bvh_ws = w;
     return v;
 }
 
@@ -482,7 +589,8 @@ extern "C" uint64_t vt_voronoi_bytes(uint32_t num_points)
     const uint32_t n = num_points, G = grid_cells_bound(n);
     return 512 + 2 * a256((size_t)(G + 1) * 4) + 2 * a256((size_t)n * 4) +
            a256((size_t)(n + 1) * 4) + 2 * a256((size_t)n * 4) + 256 +
-           a256((size_t)n * kMaxPlanes * 4) + a256(scan_bytes(n));
+           a256((size_t)n * kMaxPlanes * 4) + a256(scan_bytes(n)) + a256(vt_bvh_nodes_bytes(n)) +
+           vt_bvh_workspace_bytes(n);
 }
 
 extern "C" vt_status vt_voronoi_adjacency(const float *points, uint32_t num_points, void *workspace,
@@ -531,22 +639,18 @@ extern "C" vt_status vt_voronoi_adjacency(const float *points, uint32_t num_poin
     cub::DeviceScan::ExclusiveSum(v.temp, tb, v.cnt, v.start, (int)(G + 1), s);
     cudaMemcpyAsync(v.cnt, v.start, (G + 1) * 4, cudaMemcpyDeviceToDevice, s);
     grid_scatter<<<vt::grid_for(n, 256), 256, 0, s>>>(n, v.cell_id, v.cnt, v.sorted);
+    grid_sort<<<vt::grid_for(G, 256), 256, 0, s>>>((uint32_t)G, v.start, v.sorted);
 
-    const int ks[2] = {32, kKnnMax};
-    const uint32_t *todo = nullptr;
-    uint32_t ntodo = n;
-    uint32_t *bufs[2] = {v.retry, v.retry + a256((size_t)n * 4) / 4};
-    for (int pass = 0; pass < 3 && ntodo > 0; ++pass) {
-        uint32_t *out = bufs[pass & 1];
-        cudaMemsetAsync(v.nretry, 0, 4, s);
-        if (pass < 2)
-            cell_kernel<<<vt::grid_for(ntodo, 64), 64, 0, s>>>(points, n, g, v.start, v.sorted,
-                                                              ks[pass], box, todo, ntodo, v.nbr,
-                                                              kMaxPlanes, v.count, out, v.nretry);
-        else
-            cell_stream_kernel<<<vt::grid_for(ntodo, 64), 64, 0, s>>>(
-                points, n, g, v.start, v.sorted, box, todo, ntodo, v.nbr, kMaxPlanes, v.count,
-                out, v.nretry);
+    st = vt_bvh_build(points, n, v.bvh, vt_bvh_nodes_bytes(n), v.bvh_ws, vt_bvh_workspace_bytes(n),
+                      stream);
+    if (st != VT_OK) return st;
+    uint32_t *retry = v.retry;
+    cudaMemsetAsync(v.nretry, 0, 4, s);
+    cell_verify_kernel<<<vt::grid_for(n, 64), 64, 0, s>>>(
+        points, n, g, v.start, v.sorted, (const vt::bvh::Node *)v.bvh, vt::bvh::leaf_ids(v.bvh, n), box,
+        v.nbr, kMaxPlanes, v.count, retry, v.nretry);
+    uint32_t ntodo = 0;
+    for (int pass = 0; pass < 2; ++pass) {
         e = cudaGetLastError();
         if (e != cudaSuccess)
             return vt::set_error(VT_ERR_CUDA, "voronoi cell kernel: %s", cudaGetErrorString(e));
@@ -555,8 +659,17 @@ extern "C" vt_status vt_voronoi_adjacency(const float *points, uint32_t num_poin
         e = cudaStreamSynchronize(s);
         if (e != cudaSuccess)
             return vt::set_error(VT_ERR_CUDA, "voronoi cell kernel: %s", cudaGetErrorString(e));
-        todo = out;
+#ifdef VT_VOR_VERBOSE
+        fprintf(stderr, "voronoi pass %d: %u cells left\n", pass, nr);
+#endif
         ntodo = nr;
+        if (pass == 1 || ntodo == 0) break;
+        // fallback: sites streamed ring by ring (convex-hull cells)
+        uint32_t *out = v.retry + a256((size_t)n * 4) / 4;
+        cudaMemsetAsync(v.nretry, 0, 4, s);
+        cell_stream_kernel<<<vt::grid_for(ntodo, 64), 64, 0, s>>>(
+            points, n, g, v.start, v.sorted, box, retry, ntodo, v.nbr, kMaxPlanes, v.count, out,
+            v.nretry);
     }
     if (unconverged) *unconverged = ntodo;  // cells left empty (degenerate clipping)
     cudaMemsetAsync(v.count + n, 0, 4, s);
