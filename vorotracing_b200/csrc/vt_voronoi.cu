@@ -4,29 +4,31 @@
 // (vorotracing/cuda/__init__.py:16-46, called every 1-100 training steps,
 // vorotracing/trainer.py:354-360).  Method: each site's Voronoi cell is built
 // independently by clipping (one thread per site):
-//   1. k nearest neighbours from a uniform grid (ring search, exact k-NN);
-//   2. the cell starts as a box around the site and is clipped by the
-//      bisector planes of the neighbours in increasing distance;
-//   3. clipping stops once the next neighbour is farther than twice the
-//      farthest cell vertex (the "security radius": no farther site can cut
-//      the cell);
-//   4. the neighbours whose planes still bound the cell are the site's
+//   1. the cell starts as a box around the site (4x the scene extent) and is
+//      clipped by the bisector planes of the site's 24 nearest sites (exact
+//      k-NN from a uniform grid);
+//   2. every vertex v of the cell is then verified by the empty-ball
+//      property of Delaunay: no site may be closer to v than the cell's own
+//      site.  The ball B(v, |v - p_i|) is searched in a BVH of the sites; a
+//      site found inside it clips the cell (removing v) and verification
+//      continues over the new vertices until every ball is empty;
+//   3. the neighbours whose planes still bound the cell are the site's
 //      Voronoi neighbours.
+// The verified cell is the exact Voronoi cell (within the box), however
+// elongated: cells of sites on dense sheets are long needles whose bounding
+// sites are far away, and the ball search touches only the BVH nodes those
+// needles' vertex balls reach.  Cells of convex-hull sites are unbounded and
+// come out as their intersection with the box, so a face lying entirely
+// beyond the box is missing.
 // The cell is stored in dual form: each vertex is a triangle of three plane
 // ids (counter-clockwise seen from outside) with its position and the three
 // neighbouring triangles across its edges.  A clip removes the triangles
 // whose vertex lies beyond the plane and closes the hole with a fan of new
 // triangles around the new plane.  Coordinates are relative to the site, so
-// bisector planes are n.x = |n|^2 / 2 with n = p_j - p_i.
-//
-// Cells whose clipping does not converge within k sorted neighbours are
-// repeated with k = 128, then by streaming every site ring by ring until the
-// security radius holds (dense sheets and large cells near the hull need
-// hundreds of candidates; a convex cell does not depend on the clip order).
-// Cells of convex-hull sites are unbounded: they are truncated by a box of
-// 4x the scene extent around the site and clipped by the 16384 sites nearest
-// to their grid cell, so a face of such a cell with a farther site can be
-// missed.
+// bisector planes are n.x = |n|^2 / 2 with n = p_j - p_i.  Predicates are
+// binary32: a near-degenerate clip sequence can fail, and such cells are
+// rebuilt with 48 seed sites (another sequence), then, if that fails too,
+// by clipping with every site ring by ring around the site (up to 16384).
 #include <cub/device/device_scan.cuh>
 
 #include "vt_abi.cuh"
@@ -347,6 +349,7 @@ __device__ int knn(const float *__restrict__ p, uint32_t i, const Grid &g,
 }
 
 constexpr int kSeedK = 24;     // nearest sites clipped before verification
+constexpr int kSeedKRetry = 48;  // the same for cells whose first clip sequence failed
 constexpr int kMaxClips = 768;  // clips of one cell in verification (then the fallback)
 
 // Clip the cell by a site that cuts its vertex v (coordinates relative to
@@ -414,18 +417,21 @@ __device__ int bvh_cut(Cell &C, const float *__restrict__ p, uint32_t i, float3 
 // convex-hull site: exact inside the truncation box).  The balls are searched
 // in the sites' BVH, so long needle-shaped cells along dense sheets and far
 // vertices of hull cells cost the nodes their balls touch.  Cells whose
-// clipping fails go to the retry list.
+// clipping fails (a near-degenerate clip sequence) go to the retry list; the
+// retry seeds with more sites, which changes the sequence.
 __global__ void __launch_bounds__(64) cell_verify_kernel(
     const float *__restrict__ p, uint32_t n, Grid g, const uint32_t *__restrict__ start,
     const uint32_t *__restrict__ sorted, const bvh::Node *__restrict__ nodes,
-    const uint32_t *__restrict__ ids, float box, uint32_t *__restrict__ nbr_out, uint32_t stride,
-    uint32_t *__restrict__ count, uint32_t *__restrict__ retry, uint32_t *nretry)
+    const uint32_t *__restrict__ ids, float box, const uint32_t *__restrict__ todo, uint32_t ntodo,
+    int seedk, uint32_t *__restrict__ nbr_out, uint32_t stride, uint32_t *__restrict__ count,
+    uint32_t *__restrict__ retry, uint32_t *nretry)
 {
-    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= n) return;
-    float kd[kSeedK];
-    uint32_t ki[kSeedK];
-    const int found = knn(p, i, g, start, sorted, kSeedK, kd, ki);
+    const uint32_t t0 = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t0 >= ntodo) return;
+    const uint32_t i = todo ? todo[t0] : t0;
+    float kd[kSeedKRetry];
+    uint32_t ki[kSeedKRetry];
+    const int found = knn(p, i, g, start, sorted, min(seedk, kSeedKRetry), kd, ki);
     Cell C;
     init_box(C, box);
     const float3 q = make_float3(p[3 * i], p[3 * i + 1], p[3 * i + 2]);
@@ -644,13 +650,24 @@ extern "C" vt_status vt_voronoi_adjacency(const float *points, uint32_t num_poin
     st = vt_bvh_build(points, n, v.bvh, vt_bvh_nodes_bytes(n), v.bvh_ws, vt_bvh_workspace_bytes(n),
                       stream);
     if (st != VT_OK) return st;
-    uint32_t *retry = v.retry;
-    cudaMemsetAsync(v.nretry, 0, 4, s);
-    cell_verify_kernel<<<vt::grid_for(n, 64), 64, 0, s>>>(
-        points, n, g, v.start, v.sorted, (const vt::bvh::Node *)v.bvh, vt::bvh::leaf_ids(v.bvh, n), box,
-        v.nbr, kMaxPlanes, v.count, retry, v.nretry);
-    uint32_t ntodo = 0;
-    for (int pass = 0; pass < 2; ++pass) {
+    uint32_t *bufs[2] = {v.retry, v.retry + a256((size_t)n * 4) / 4};
+    const vt::bvh::Node *nodes = (const vt::bvh::Node *)v.bvh;
+    const uint32_t *ids = vt::bvh::leaf_ids(v.bvh, n);
+    const uint32_t *todo = nullptr;
+    uint32_t ntodo = n;
+    // pass 0: every cell; pass 1: failures, seeded with more sites; pass 2:
+    // remaining failures, sites streamed ring by ring
+    for (int pass = 0; pass < 3 && ntodo > 0; ++pass) {
+        uint32_t *out = bufs[pass & 1];
+        cudaMemsetAsync(v.nretry, 0, 4, s);
+        if (pass < 2)
+            cell_verify_kernel<<<vt::grid_for(ntodo, 64), 64, 0, s>>>(
+                points, n, g, v.start, v.sorted, nodes, ids, box, todo, ntodo,
+                pass == 0 ? kSeedK : kSeedKRetry, v.nbr, kMaxPlanes, v.count, out, v.nretry);
+        else
+            cell_stream_kernel<<<vt::grid_for(ntodo, 64), 64, 0, s>>>(
+                points, n, g, v.start, v.sorted, box, todo, ntodo, v.nbr, kMaxPlanes, v.count,
+                out, v.nretry);
         e = cudaGetLastError();
         if (e != cudaSuccess)
             return vt::set_error(VT_ERR_CUDA, "voronoi cell kernel: %s", cudaGetErrorString(e));
@@ -660,16 +677,10 @@ extern "C" vt_status vt_voronoi_adjacency(const float *points, uint32_t num_poin
         if (e != cudaSuccess)
             return vt::set_error(VT_ERR_CUDA, "voronoi cell kernel: %s", cudaGetErrorString(e));
 #ifdef VT_VOR_VERBOSE
-        fprintf(stderr, "voronoi pass %d: %u cells left\n", pass, nr);
+        fprintf(stderr, "voronoi pass %d: %u cells in, %u left\n", pass, ntodo, nr);
 #endif
+        todo = out;
         ntodo = nr;
-        if (pass == 1 || ntodo == 0) break;
-        // fallback: sites streamed ring by ring (convex-hull cells)
-        uint32_t *out = v.retry + a256((size_t)n * 4) / 4;
-        cudaMemsetAsync(v.nretry, 0, 4, s);
-        cell_stream_kernel<<<vt::grid_for(ntodo, 64), 64, 0, s>>>(
-            points, n, g, v.start, v.sorted, box, retry, ntodo, v.nbr, kMaxPlanes, v.count, out,
-            v.nretry);
     }
     if (unconverged) *unconverged = ntodo;  // cells left empty (degenerate clipping)
     cudaMemsetAsync(v.count + n, 0, 4, s);
