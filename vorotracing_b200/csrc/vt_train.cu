@@ -174,8 +174,22 @@ __global__ void __launch_bounds__(kTrainBlock, VT_BWD_MIN_BLOCKS)
     oct_encode<R>(mk(-ray.d.x, -ray.d.y, -ray.d.z), tu, tv);
     I.spec = make_bilin<R>(tu, tv);
     if (M == kBwdReplay) {
+        WalkState w;
         walk_replay<BwdInteg<AT, R, F>>(ray, a.points, a.density, start, min(L, a.max_steps), I,
-                                        b.rec.cells + r, b.rec.stride);
+                                        b.rec.cells + r, b.rec.stride, w);
+    } else if (M == kBwdWalkFlagged) {
+        // replay what the record holds, then walk on with the face scan
+        WalkState w;
+        const uint32_t Lr = min(min(L & ~kPathWalk, b.rec.cap), a.max_steps);
+        if (walk_replay<BwdInteg<AT, R, F>>(ray, a.points, a.density, start, Lr, I,
+                                            b.rec.cells + r, b.rec.stride, w)) {
+            w.begin = __ldg(a.offs + w.cur);
+            w.deg = __ldg(a.offs + w.cur + 1) - w.begin;
+            WalkDebug none{nullptr, 0, nullptr, nullptr, nullptr, nullptr};
+            walk_from<BwdInteg<AT, R, F>, false, false>(w, ray, a.faces, a.points, a.density,
+                                                         a.max_steps, I, r, none,
+                                                         PathRec{nullptr, 0, 0, nullptr});
+        }
     } else {
         WalkDebug none{nullptr, 0, nullptr, nullptr, nullptr, nullptr};
         walk<BwdInteg<AT, R, F>, false>(ray, a.faces, a.offs, a.points, a.density, start,

@@ -220,14 +220,16 @@ constexpr uint32_t kPathWalk = 0x80000000u;
 // sites).  The walk is deterministic, so every recorded step is the step the
 // scan would take, and an unflagged record ends where the backward's walk
 // ends (no exit face, the step limit, or T < weight_threshold, which stopped
-// the forward at the same step).  Flagged rays are skipped here and walked
-// by a second launch.  The record of step k+2 and the site of step k+1 are
-// loaded one iteration ahead.
+// the forward at the same step).  Returns false if the integrator stopped the
+// walk, else true with w set to the walk state after the recorded steps
+// (begin / deg left for the caller), from which a flagged ray's walk goes on.
+// The record of step k+2 and the site of step k+1 are loaded one iteration
+// ahead.
 template <class Integ>
-__device__ __forceinline__ void walk_replay(const Ray &ray, const float *__restrict__ points,
+__device__ __forceinline__ bool walk_replay(const Ray &ray, const float *__restrict__ points,
                                             const float *__restrict__ density, uint32_t start,
                                             uint32_t L, Integ &I, const uint32_t *cells,
-                                            uint64_t stride)
+                                            uint64_t stride, WalkState &w)
 {
     uint32_t cur = start;
     V3 P = ld3(points + (size_t)start * 3);
@@ -252,7 +254,7 @@ __device__ __forceinline__ void walk_replay(const Ray &ray, const float *__restr
         }
         if (k + 2 < L) nb2 = __ldg(cells + (uint64_t)(k + 2) * stride);
         const float t1 = face_exit_t(P, Q, ray);
-        if (t1 > t0 && !I.integrate(cur, t0, t1, P, Q, s)) return;
+        if (t1 > t0 && !I.integrate(cur, t0, t1, P, Q, s)) return false;
         t0 = fmaxf(t0, t1);
         cur = nb;
         P = Q;
@@ -262,6 +264,12 @@ __device__ __forceinline__ void walk_replay(const Ray &ray, const float *__restr
         sq = sqn;
         nb1 = nb2;
     }
+    w.cur = cur;
+    w.P = P;
+    w.s = s;
+    w.t0 = t0;
+    w.n = L;
+    return true;
 }
 
 }  // namespace vt
