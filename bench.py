@@ -99,17 +99,18 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def load_scene(rank: int, ws: int, name: str = "C2", adjacency: str = "qhull"):
-    """Scene arrays of a configuration; rank 0 builds the adjacency cache first."""
+def load_scene(rank: int, ws: int, name: str = "C2", adjacency: str = "qhull", n=None):
+    """Scene arrays of a configuration (``n`` overrides the site count, for
+    small profiling captures); rank 0 builds the adjacency cache first."""
     from vorotracing_b200 import scene as sc
 
     if ws > 1:
         import torch.distributed as dist
 
         if rank == 0:
-            sc.config_scene(name, adjacency=adjacency)
+            sc.config_scene(name, n=n, adjacency=adjacency)
         dist.barrier()
-    return sc.config_scene(name, adjacency=adjacency)
+    return sc.config_scene(name, n=n, adjacency=adjacency)
 
 
 def compulsory_bytes(scene, rays, start, dbg_ops):
@@ -217,7 +218,10 @@ def main():
     ap.add_argument("--config", default="C2", choices=["C2", "C3", "C4", "C5"],
                     help="C2 (default, the headline) or another benchmark configuration")
     ap.add_argument("--profile", action="store_true",
-                    help="a few untimed renders only (for ncu captures)")
+                    help="a few untimed steps only (for ncu captures)")
+    ap.add_argument("--sites", type=int, default=None,
+                    help="override the configuration's site count (small ncu captures of "
+                         "--config C4; never for a reported number)")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)

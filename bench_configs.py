@@ -121,7 +121,7 @@ def run_c3(args, ws, rank, dev):
 def run_c4(args, ws, rank, dev):
     from vorotracing_b200.cuda import _ops
 
-    s = bench.load_scene(rank, ws, "C4", adjacency="gpu")
+    s = bench.load_scene(rank, ws, "C4", adjacency="gpu", n=args.sites)
     t = _scene_tensors(s, dev)
     W, H = sc.CONFIGS["C4"]["W"], sc.CONFIGS["C4"]["H"]
     rays = torch.from_numpy(sc.pinhole_rays(sc.intrinsics(W, H), sc.orbit_pose(rank, 64), W, H)).to(dev)
@@ -162,6 +162,11 @@ def run_c4(args, ws, rank, dev):
                                    grads=bucket.views(), path=path)
         bucket.allreduce_()
 
+    if args.profile:
+        for _ in range(3):
+            step()
+        torch.cuda.synchronize()
+        return
     ms, clocks = Timer(args, dev).run(step, ws)
     if rank == 0:
         rays_total = nr * ws * args.steps
