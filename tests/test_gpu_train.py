@@ -202,8 +202,11 @@ def test_bwd_into_flat_bucket(c1_scene, c1_rays):
     ref = _ops.trace_vorotracing_bwd(*args, *common)
     b = GradBucket(g["points"].size(0), g["diffuse"].size(1), "cuda")
     _ops.trace_vorotracing_bwd(*args, *common, grads=b.views())
+    # same kernels, different destination: equal up to the order of the fp32
+    # atomic additions (sums of many terms with cancellation)
     for got, want in zip(b.views(), (ref[0], ref[1], ref[2], ref[3])):
-        torch.testing.assert_close(got.reshape(want.shape), want, rtol=1e-5, atol=1e-6)
+        scale = float(want.abs().max()) if want.numel() else 1.0
+        torch.testing.assert_close(got.reshape(want.shape), want, rtol=1e-4, atol=1e-5 * scale)
 
 
 @pytest.mark.parametrize("half", [False, True])
