@@ -160,6 +160,7 @@ __global__ void __launch_bounds__(kTrainBlock, VT_BWD_MIN_BLOCKS)
     I.dgr = b.dist_grad ? b.dist_grad[r] : 0.0f;
     I.Dt = (2.0f * fd) * I.dgr;
     I.Drun = 0.0f;
+    I.s_prev = 0.0f;
     I.pgrad = b.points_grad;
     I.ddiff = b.diffuse_grad;
     I.dspec = b.specular_grad;

@@ -69,6 +69,7 @@ template <class AT, int R> struct FwdInteg {
     float *qdepth;
     uint32_t *qidx;
     float W, S, dist, self, tfar;
+    float s_prev;  // 1 - 1/(1 + t0) of the current t0 (the previous segment's s1)
     AT *contrib;
 
     __device__ __forceinline__ FwdInteg(const Ray &r, const TexPlain<AT, R> &t, float wt_,
@@ -76,7 +77,7 @@ template <class AT, int R> struct FwdInteg {
                                         uint32_t *qidx_, AT *contrib_)
         : ray(r), tex(t), wt(wt_), acc(mk(0.f, 0.f, 0.f)), T(1.0f), ntex(0), qthr(qthr_), K(K_),
           qi(0), qv(0.0f), qdepth(qdepth_), qidx(qidx_), W(0.f), S(0.f), dist(0.f), self(0.f),
-          tfar(0.f), contrib(contrib_)
+          tfar(0.f), s_prev(0.f), contrib(contrib_)
     {
         if (K > 0) qv = qthr[0];
         float tu, tv;
@@ -100,8 +101,12 @@ template <class AT, int R> struct FwdInteg {
         float delta = fmaxf(t1 - t0, 0.0f);
         float alpha = 1.0f - expf_exact(-s * delta);
         float w = T * alpha;
-        float s0 = 1.0f - 1.0f / (1.0f + t0);
+        // the walk integrates [t0, t1] only for t1 > t0 and then sets t0 = t1,
+        // so this segment's t0 is the previous one's t1 (0 before the first)
+        // and its s value was already computed: 1 - 1/(1 + 0) = 0 to start
+        float s0 = s_prev;
         float s1 = 1.0f - 1.0f / (1.0f + t1);
+        s_prev = s1;
         float mid = 0.5f * (s0 + s1);
         float ds = s1 - s0;
         dist = fmaf(w, fmaf(mid, W, -S), dist);
@@ -162,6 +167,7 @@ template <class AT, int R, int F = kBwdDepth | kBwdDist | kBwdErr> struct BwdInt
     uint32_t K, qi;
     float qv, cur_dg, ray_error;
     float W, S, Wt, St, dgr, Dt, Drun;
+    float s_prev;
     float *pgrad;
     AT *ddiff, *dspec;
     // Optional padded fp32 scratch: one float4 per texel / site, accumulated
@@ -236,8 +242,9 @@ template <class AT, int R, int F = kBwdDepth | kBwdDist | kBwdErr> struct BwdInt
         float dLddt = dLda * dadd;
         float dLdt0 = 0.0f;
         if ((F & kBwdDist) != 0 && dgr != 0.0f) {
-            float s0 = 1.0f - 1.0f / (1.0f + t0);
+            float s0 = s_prev;  // as in FwdInteg: the previous segment's s1
             float s1 = 1.0f - 1.0f / (1.0f + t1);
+            s_prev = s1;
             float mid = 0.5f * (s0 + s1);
             float ds = s1 - s0;
             float Wm = W, Sm = S;
