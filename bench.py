@@ -8,14 +8,15 @@ textures, Morton-sorted cells, 4x8 warp tiles, one 1296x840 pinhole view per
 GPU (rank r renders orbit view r), weight_threshold 0.01, cell_skip 1e-3.
 A step = start-cell lookup + full-frame traversal render.  Scene arrays are
 resident in HBM before timing; L2 is flushed (256 MB write) between timed
-steps.  `e2e` renders through InferScene.render_host from pinned host rays,
-with the host<->device copies inside the timed region.
+steps.  `e2e` renders through InferScene.render_host from page-locked host
+rays to page-locked host rgba, the bus transfers inside the timed region (by
+default the trace kernel reads and writes host memory directly).
 
 Multi-GPU: one process per GPU (torchrun), the scene is replicated, views are
 independent (weak scaling, no collective on the data path); time = max over
 ranks.  --impl reference times the CPU restatement of the reference's
-algorithm (the reference's own CUDA extension cannot be built; see
-DESIGN.md) on all host cores, rank 0 only.
+algorithm (the reference's own CUDA extension cannot be built: its Eigen
+and cuBQL submodules are empty) on all host cores, rank 0 only.
 """
 from __future__ import annotations
 

@@ -179,4 +179,6 @@ def _foam_golden(root: str, vv):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) < 2:
+        sys.exit("usage: make_golden.py <path to the VoroTracing checkout>")
+    main(sys.argv[1])
