@@ -204,8 +204,10 @@ def run_c5(args, ws, rank, dev):
     frames = []
     for cam in (fe, rs, tl):
         r = cam.rays(dev).index_select(0, rows).contiguous()
-        frames.append(r.reshape(-1, 6))
-    nr = sum(f.size(0) for f in frames)
+        # image-shaped (rows, W * spp, 6): the render then traces in 4x8 warp
+        # tiles (the lens samples of a pixel are adjacent columns)
+        frames.append(r.reshape(r.size(0), -1, 6))
+    nr = sum(f.numel() // 6 for f in frames)
 
     def step():
         for r in frames:

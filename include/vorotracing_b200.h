@@ -259,8 +259,14 @@ VT_API uint64_t vt_voronoi_bytes(uint32_t num_points);
  * offsets (num_points + 1, device) and returns the entry count on the host
  * (*num_entries); neighbour ids of each row are ascending.  *unconverged
  * (host, optional) = cells left empty after every pass.  Synchronises the
- * stream (it reads sizes back to the host). */
-VT_API vt_status vt_voronoi_adjacency(const float *points, uint32_t num_points, void *workspace,
+ * stream (it reads sizes back to the host).  seed_adjacency / seed_offsets
+ * (device CSR, optional, both or neither): initial guesses of each site's
+ * neighbours (e.g. the adjacency before the sites moved, as paragram's
+ * initial_guesses); they replace the nearest-site seeding and do not change
+ * the result, which every cell's vertex verification fixes. */
+VT_API vt_status vt_voronoi_adjacency(const float *points, uint32_t num_points,
+                                      const uint32_t *seed_adjacency, const uint32_t *seed_offsets,
+                                      void *workspace,
                                       uint64_t workspace_bytes, uint32_t *offsets,
                                       uint64_t *num_entries, uint32_t *unconverged,
                                       vt_stream stream);

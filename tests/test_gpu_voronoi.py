@@ -66,3 +66,22 @@ def test_render_with_gpu_adjacency():
     rb = b.render(rays, weight_threshold=0.01).float()
     close = (ra - rb).abs().max(-1).values < 1e-2
     assert close.float().mean().item() > 0.999
+
+
+def test_seeded_build_matches_unseeded():
+    """Initial guesses (the adjacency before the sites moved) only change the
+    clipping order: the verified cells, hence the rows, are the same."""
+    from vorotracing_b200 import scene as sc
+    from vorotracing_b200.cuda import build_voronoi_adjacency
+
+    pts = sc.make_sites(30000, 7, plane=True)
+    moved = pts + np.random.default_rng(1).normal(0, 1e-3, pts.shape).astype(np.float32)
+    d = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    a0, o0, _ = build_voronoi_adjacency(d(pts))
+    a1, o1, s1 = build_voronoi_adjacency(d(moved))
+    a2, o2, s2 = build_voronoi_adjacency(d(moved), initial_guesses=a0, initial_guesses_offsets=o0)
+    assert int(s1[0]) == 0 and int(s2[0]) == 0
+    o1, a1, o2, a2 = (t.cpu().numpy() for t in (o1, a1, o2, a2))
+    same = np.mean([np.array_equal(a1[o1[i]:o1[i + 1]], a2[o2[i]:o2[i + 1]])
+                    for i in range(len(pts))])
+    assert same >= 0.9999, same

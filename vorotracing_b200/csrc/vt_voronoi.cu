@@ -423,7 +423,8 @@ __global__ void __launch_bounds__(64) cell_verify_kernel(
     const float *__restrict__ p, uint32_t n, Grid g, const uint32_t *__restrict__ start,
     const uint32_t *__restrict__ sorted, const bvh::Node *__restrict__ nodes,
     const uint32_t *__restrict__ ids, float box, const uint32_t *__restrict__ todo, uint32_t ntodo,
-    int seedk, uint32_t *__restrict__ nbr_out, uint32_t stride, uint32_t *__restrict__ count,
+    int seedk, const uint32_t *__restrict__ seed_adj, const uint32_t *__restrict__ seed_offs,
+    uint32_t *__restrict__ nbr_out, uint32_t stride, uint32_t *__restrict__ count,
     uint32_t *__restrict__ retry, uint32_t *nretry)
 {
     const uint32_t t0 = blockIdx.x * blockDim.x + threadIdx.x;
@@ -431,7 +432,28 @@ __global__ void __launch_bounds__(64) cell_verify_kernel(
     const uint32_t i = todo ? todo[t0] : t0;
     float kd[kSeedKRetry];
     uint32_t ki[kSeedKRetry];
-    const int found = knn(p, i, g, start, sorted, min(seedk, kSeedKRetry), kd, ki);
+    int found = 0;
+    if (seed_adj) {
+        // the caller's guesses, nearest first (up to kSeedKRetry of them)
+        const float3 qi = make_float3(p[3 * i], p[3 * i + 1], p[3 * i + 2]);
+        const uint32_t b = seed_offs[i], e = seed_offs[i + 1];
+        for (uint32_t k = b; k < e && found < kSeedKRetry; ++k) {
+            const uint32_t j = seed_adj[k];
+            if (j >= n || j == i) continue;
+            const float dx = p[3 * j] - qi.x, dy = p[3 * j + 1] - qi.y, dz = p[3 * j + 2] - qi.z;
+            const float d2 = dx * dx + dy * dy + dz * dz;
+            int pos = found++;
+            while (pos > 0 && kd[pos - 1] > d2) {
+                kd[pos] = kd[pos - 1];
+                ki[pos] = ki[pos - 1];
+                --pos;
+            }
+            kd[pos] = d2;
+            ki[pos] = j;
+        }
+    } else {
+        found = knn(p, i, g, start, sorted, min(seedk, kSeedKRetry), kd, ki);
+    }
     Cell C;
     init_box(C, box);
     const float3 q = make_float3(p[3 * i], p[3 * i + 1], p[3 * i + 2]);
@@ -599,7 +621,9 @@ extern "C" uint64_t vt_voronoi_bytes(uint32_t num_points)
            vt_bvh_workspace_bytes(n);
 }
 
-extern "C" vt_status vt_voronoi_adjacency(const float *points, uint32_t num_points, void *workspace,
+extern "C" vt_status vt_voronoi_adjacency(const float *points, uint32_t num_points,
+                                          const uint32_t *seed_adjacency,
+                                          const uint32_t *seed_offsets, void *workspace,
                                           uint64_t workspace_bytes, uint32_t *offsets,
                                           uint64_t *num_entries, uint32_t *unconverged,
                                           vt_stream stream)
@@ -607,6 +631,8 @@ extern "C" vt_status vt_voronoi_adjacency(const float *points, uint32_t num_poin
     const uint32_t n = num_points;
     VT_REQUIRE(points && workspace && offsets && num_entries, "vt_voronoi_adjacency: null pointer");
     VT_REQUIRE(n >= 2, "vt_voronoi_adjacency: need at least 2 sites");
+    VT_REQUIRE(!seed_adjacency == !seed_offsets,
+               "vt_voronoi_adjacency: seed adjacency and offsets go together");
     VT_REQUIRE(workspace_bytes >= vt_voronoi_bytes(n) && ((uintptr_t)workspace & 255u) == 0,
                "vt_voronoi_adjacency: workspace must be vt_voronoi_bytes large, 256-byte aligned");
     cudaStream_t s = (cudaStream_t)stream;
@@ -663,7 +689,8 @@ extern "C" vt_status vt_voronoi_adjacency(const float *points, uint32_t num_poin
         if (pass < 2)
             cell_verify_kernel<<<vt::grid_for(ntodo, 64), 64, 0, s>>>(
                 points, n, g, v.start, v.sorted, nodes, ids, box, todo, ntodo,
-                pass == 0 ? kSeedK : kSeedKRetry, v.nbr, kMaxPlanes, v.count, out, v.nretry);
+                pass == 0 ? kSeedK : kSeedKRetry, pass == 0 ? seed_adjacency : nullptr,
+                seed_offsets, v.nbr, kMaxPlanes, v.count, out, v.nretry);
         else
             cell_stream_kernel<<<vt::grid_for(ntodo, 64), 64, 0, s>>>(
                 points, n, g, v.start, v.sorted, box, todo, ntodo, v.nbr, kMaxPlanes, v.count,

@@ -643,13 +643,27 @@ def build_voronoi_adjacency(points, *, debug: bool = False, initial_guesses=None
     around paragram, vorotracing/cuda/__init__.py:16-46): returns (adjacency
     uint32 with ``chunk_padding`` zero entries at the tail, offsets uint32
     (N+1), status int32 tensor [cells left without neighbours]).
-    ``debug`` and the initial-guess arguments are accepted for signature
-    compatibility; the clipping method needs no initial guesses."""
-    del debug, initial_guesses, initial_guesses_offsets
+    ``initial_guesses`` / ``initial_guesses_offsets`` (a CSR of guessed
+    neighbours, e.g. the adjacency before the sites moved) seed the cells'
+    clipping instead of the nearest sites; the result does not depend on
+    them.  ``debug`` is accepted for signature compatibility."""
+    del debug
     pts = points.detach().contiguous()
     if pts.device.type != "cuda" or pts.dtype != torch.float32 or pts.dim() != 2 or pts.size(1) != 3:
         _fail("points must be a float32 (N, 3) CUDA tensor")
     n = pts.size(0)
+    seed_a = seed_o = None
+    if (initial_guesses is None) != (initial_guesses_offsets is None):
+        _fail("initial_guesses and initial_guesses_offsets go together")
+    if initial_guesses is not None:
+        seed_a = initial_guesses.to(device=pts.device).contiguous()
+        seed_o = initial_guesses_offsets.to(device=pts.device).contiguous()
+        if seed_o.numel() != n + 1:
+            _fail("initial_guesses_offsets must have num_points + 1 entries")
+        if seed_a.dtype not in (torch.int32, torch.uint32):
+            seed_a = seed_a.to(torch.int32)
+        if seed_o.dtype not in (torch.int32, torch.uint32):
+            seed_o = seed_o.to(torch.int32)
     L = lib()
     L.vt_voronoi_bytes.restype = C.c_uint64
     wb = int(L.vt_voronoi_bytes(C.c_uint32(n)))
@@ -658,7 +672,8 @@ def build_voronoi_adjacency(points, *, debug: bool = False, initial_guesses=None
     E = C.c_uint64(0)
     bad = C.c_uint32(0)
     stream = stream_ptr(pts.device)
-    check(L.vt_voronoi_adjacency(ptr(pts), C.c_uint32(n), ptr(ws), C.c_uint64(wb), ptr(offs),
+    check(L.vt_voronoi_adjacency(ptr(pts), C.c_uint32(n), ptr(seed_a), ptr(seed_o), ptr(ws),
+                                 C.c_uint64(wb), ptr(offs),
                                  C.byref(E), C.byref(bad), stream), "vt_voronoi_adjacency")
     adj = torch.zeros(int(E.value) + chunk_padding, dtype=torch.int32, device=pts.device)
     check(L.vt_voronoi_write(ptr(ws), C.c_uint32(n), ptr(offs), ptr(adj), stream),
