@@ -249,6 +249,15 @@ VT_API vt_status vt_bvh_build_noalloc(const float *points, uint32_t num_points, 
 VT_API vt_status vt_bvh_query(const void *nodes, const float *points, uint32_t num_points,
                               const float *queries, uint32_t num_queries, int32_t *out,
                               uint32_t *err, vt_stream stream);
+/* vt_bvh_query with a hint: hint (device, hint_count = 1 for all queries or
+ * num_queries) names a site believed nearest, which bounds the search from
+ * the start; the answer is the same.  Per-ray start cells of cameras whose
+ * origins share a cell (rolling shutter, thin lens) cost a fraction of the
+ * unhinted search.  No reference counterpart. */
+VT_API vt_status vt_bvh_query_hint(const void *nodes, const float *points, uint32_t num_points,
+                                   const float *queries, uint32_t num_queries,
+                                   const uint32_t *hint, uint32_t hint_count, int32_t *out,
+                                   uint32_t *err, vt_stream stream);
 
 /* ---- Voronoi adjacency (replaces the external paragram package,
  *      vorotracing/cuda/__init__.py:16-46) ---- */

@@ -25,7 +25,13 @@ def test_bvh_matches_brute_force(c1_scene):
     b = NNBVH()
     b.build(_dev(pts))
     got = b.query(_dev(pts), _dev(q)).cpu().numpy()
-    np.testing.assert_array_equal(got, oracle.nn_query(pts, q))
+    ref = oracle.nn_query(pts, q)
+    np.testing.assert_array_equal(got, ref)
+    # a hint (good, bad, or one per query) never changes the answer
+    for hint in (torch.tensor([int(ref[0])]), torch.tensor([12345]),
+                 torch.from_numpy(rng.integers(0, len(pts), len(q)).astype(np.int32))):
+        got = b.query(_dev(pts), _dev(q), hint=hint.cuda()).cpu().numpy()
+        np.testing.assert_array_equal(got, ref)
 
 
 @pytest.mark.parametrize("n", [1, 2, 3, 33])
@@ -36,7 +42,14 @@ def test_bvh_tiny_and_duplicates(n):
     pts = rng.integers(0, 2, (n, 3)).astype(np.float32)  # duplicates for n > 8
     q = rng.uniform(-1, 2, (257, 3)).astype(np.float32)
     got = nearest_neighbor_bvh(_dev(pts), _dev(q)).cpu().numpy()
-    np.testing.assert_array_equal(got, oracle.nn_query(pts, q))
+    ref = oracle.nn_query(pts, q)
+    np.testing.assert_array_equal(got, ref)
+    from vorotracing_b200.cuda import NNBVH
+
+    b = NNBVH()
+    b.build(_dev(pts))
+    hint = torch.tensor([n - 1], dtype=torch.int32).cuda()  # ties must still go to the lowest id
+    np.testing.assert_array_equal(b.query(_dev(pts), _dev(q), hint=hint).cpu().numpy(), ref)
 
 
 @pytest.mark.parametrize("quant", ["fp16", "q8"])

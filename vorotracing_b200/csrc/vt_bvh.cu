@@ -176,9 +176,13 @@ __device__ __forceinline__ void visit_leaf(const float *__restrict__ p, uint32_t
     }
 }
 
+// A hint (a site believed nearest, e.g. the answer for a neighbouring query)
+// only seeds the bound: the result is the same lexicographic (d2, id) minimum,
+// found with tighter pruning when the hint is good.
 __global__ void query_kernel(const Node *__restrict__ nodes, const uint32_t *__restrict__ ids,
                              const float *__restrict__ p, uint32_t n,
-                             const float *__restrict__ queries, uint32_t nq, int32_t *out,
+                             const float *__restrict__ queries, uint32_t nq,
+                             const uint32_t *__restrict__ hint, uint32_t hint_count, int32_t *out,
                              uint32_t *err)
 {
     uint32_t t = blockIdx.x * blockDim.x + threadIdx.x;
@@ -187,6 +191,10 @@ __global__ void query_kernel(const Node *__restrict__ nodes, const uint32_t *__r
               __ldg(queries + (size_t)t * 3 + 2));
     float best = __int_as_float(0x7f800000);
     uint32_t bi = 0xffffffffu;
+    if (hint) {
+        const uint32_t h = __ldg(hint + (hint_count == 1 ? 0 : t));
+        if (h < n) visit_leaf(p, h, q, best, bi);
+    }
     if (n == 1) {
         visit_leaf(p, 0, q, best, bi);
         out[t] = (int32_t)bi;
@@ -331,8 +339,27 @@ extern "C" vt_status vt_bvh_query(const void *nodes, const float *points, uint32
     const uint32_t *ids =
         (const uint32_t *)((const char *)nodes + align256((size_t)(num_points - 1) * sizeof(Node)));
     vt::bvh::query_kernel<<<vt::grid_for(num_queries, 128), 128, 0, (cudaStream_t)stream>>>(
-        nd, ids, points, num_points, queries, num_queries, out, err);
+        nd, ids, points, num_points, queries, num_queries, nullptr, 0, out, err);
     return vt::check_launch("vt_bvh_query");
+}
+
+extern "C" vt_status vt_bvh_query_hint(const void *nodes, const float *points, uint32_t num_points,
+                                       const float *queries, uint32_t num_queries,
+                                       const uint32_t *hint, uint32_t hint_count, int32_t *out,
+                                       uint32_t *err, vt_stream stream)
+{
+    VT_REQUIRE(nodes && points && num_points > 0,
+               "vt_bvh_query_hint: BVH must be built before querying");
+    VT_REQUIRE(num_queries == 0 || (queries && out), "vt_bvh_query_hint: null query buffers");
+    VT_REQUIRE(hint && (hint_count == 1 || hint_count == num_queries),
+               "vt_bvh_query_hint: hint must hold 1 or num_queries site ids");
+    if (num_queries == 0) return VT_OK;
+    const Node *nd = (const Node *)nodes;
+    const uint32_t *ids =
+        (const uint32_t *)((const char *)nodes + align256((size_t)(num_points - 1) * sizeof(Node)));
+    vt::bvh::query_kernel<<<vt::grid_for(num_queries, 128), 128, 0, (cudaStream_t)stream>>>(
+        nd, ids, points, num_points, queries, num_queries, hint, hint_count, out, err);
+    return vt::check_launch("vt_bvh_query_hint");
 }
 
 // ---------------------------------------------------------------------------

@@ -296,7 +296,10 @@ class NNBVH:
         self._ws_keep = ws  # freed on the next build; the stream orders reuse
         self.num_points = n
 
-    def query(self, points, queries):
+    def query(self, points, queries, hint=None):
+        """Nearest site per query (int32).  ``hint``: optional site id(s) (a
+        1-element or per-query tensor) believed nearest; it only speeds up the
+        search."""
         if self._nodes is None:
             _fail("BVH must be built before querying")
         if queries.device.type != "cuda":
@@ -306,9 +309,21 @@ class NNBVH:
             _fail("points must be the point set the BVH was built on")
         q = queries.detach().reshape(-1, 3).contiguous().float()
         out = torch.empty(q.size(0), dtype=torch.int32, device=q.device)
-        check(lib().vt_bvh_query(ptr(self._nodes), ptr(points), C.c_uint32(self.num_points),
-                                 ptr(q), C.c_uint32(q.size(0)), ptr(out), None,
-                                 stream_ptr(q.device)), "vt_bvh_query")
+        if hint is None:
+            check(lib().vt_bvh_query(ptr(self._nodes), ptr(points), C.c_uint32(self.num_points),
+                                     ptr(q), C.c_uint32(q.size(0)), ptr(out), None,
+                                     stream_ptr(q.device)), "vt_bvh_query")
+            return out
+        h = hint.detach().reshape(-1).to(device=q.device)
+        if h.dtype not in (torch.int32, torch.uint32):
+            h = h.to(torch.int32)
+        h = h.contiguous()
+        if h.numel() not in (1, q.size(0)):
+            _fail("hint must hold 1 or one site id per query")
+        check(lib().vt_bvh_query_hint(ptr(self._nodes), ptr(points), C.c_uint32(self.num_points),
+                                      ptr(q), C.c_uint32(q.size(0)), ptr(h),
+                                      C.c_uint32(h.numel()), ptr(out), None,
+                                      stream_ptr(q.device)), "vt_bvh_query_hint")
         return out
 
 

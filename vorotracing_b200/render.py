@@ -69,7 +69,10 @@ class InferScene:
         lead = rays.shape[:-1]
         flat = rays.reshape(-1, rays.shape[-1])
         if per_ray:
-            idx = self.bvh.query(self.primal_points, flat[:, :3])
+            # the first origin's cell bounds every ray's search (origins of a
+            # moving or thick-lens camera stay close together)
+            first = self.bvh.query(self.primal_points, flat[:1, :3])
+            idx = self.bvh.query(self.primal_points, flat[:, :3], hint=first)
             return idx.view(torch.uint32).reshape(lead)
         idx = self.bvh.query(self.primal_points, flat[:1, :3])
         return idx.expand(flat.shape[0]).reshape(lead).contiguous().view(torch.uint32)
