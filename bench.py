@@ -332,9 +332,22 @@ def main():
         hbm, peak_src = 6650.0, "fallback"
     achieved = comp / (trace_ms * 1e-3) / 1e9
     traffic = None
+    warp_inst = None
     prof = os.path.join(ROOT, "profiles", "trace_infer_f16_c2.json")
     if os.path.exists(prof):
-        traffic = json.load(open(prof)).get("dram_bytes_per_launch")
+        pj = json.load(open(prof))
+        traffic = pj.get("dram_bytes_per_launch")
+        warp_inst = pj.get("warp_instructions_per_launch")
+    issue = None
+    if warp_inst:
+        # the kernel is instruction-issue bound: one warp instruction per cycle
+        # per SM sub-partition (4 per SM, 148 SMs) at the sampled SM clock
+        sm_hz = float(clocks.get("sm_mhz") or 1965.0) * 1e6
+        peak_issue = 148 * 4 * sm_hz
+        got_issue = warp_inst / (trace_ms * 1e-3)
+        issue = {"achieved": got_issue, "peak": peak_issue, "unit": "warp instructions/s",
+                 "frac": got_issue / peak_issue, "warp_instructions_per_launch": warp_inst,
+                 "source": "ncu smsp__inst_executed.sum of the same kernel (profiles/)"}
     out = {
         "metric": METRIC, "value": value, "unit": "Mrays/s", "n_gpus": ws, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": step_ms / args.steps,
@@ -357,6 +370,7 @@ def main():
                      "algorithmic_bytes_per_launch": comp,
                      "kernel": "vt::infer_kernel<8, TexF16x4<8>>",
                      "kernel_ms": trace_ms},
+        "issue_roofline": issue,
         "traversal": stats,
         "clocks": clocks,
         # value loop: BVH query + trace; e2e loop: one BVH query + one trace per band
