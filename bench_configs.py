@@ -144,8 +144,9 @@ def run_c4(args, ws, rank, dev):
     n = t["points"].size(0)
     bucket = GradBucket(n, t["diffuse"].size(1), dev)
     nr = H * W
-    # the forward records each ray's first 256 cells; the backward replays
-    # them without scanning faces (1 KB per ray)
+    # the forward records each ray's first 256 steps (cell + segment colour);
+    # the backward replays them without scanning faces or re-reading texels
+    # (4 KB per ray)
     path = ops_.PathRecord(nr, 256, dev)
 
     def step():
@@ -174,7 +175,7 @@ def run_c4(args, ws, rank, dev):
               rays_total / (ms * 1e-3), "rays/s", ms, clocks,
               {"workload": "C4: 3M-site fp32 scene, R=8, one 1552x1040 camera per GPU vs a "
                            "seeded U(0,1) target, MSE; step = face pack + fwd (recording each "
-                           "ray's first 256 cells) + bwd (replaying them) + NCCL "
+                           "ray's first 256 steps: cell + colour) + bwd (replaying them) + NCCL "
                            "all-reduce of the flat fp32 gradient bucket; optimizer excluded",
                "sites": n, "rays_per_step_per_gpu": nr,
                "grad_bucket_bytes": bucket.nbytes,

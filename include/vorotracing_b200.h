@@ -132,20 +132,23 @@ VT_API vt_status vt_trace_depth(const vt_scene *scene, const float *rays, uint32
 
 /* ---- training ---- */
 
-/* Path record: the training forward stores, for each ray, the cell it enters
- * at every walk step (cells (cap, num_rays) u32, slot-major: cells[k *
- * num_rays + r]) and the number of steps that found an exit face (len
- * (num_rays) u32; steps beyond cap are not stored).  Bit 31 of len flags a
- * ray that the backward must walk itself: the record overflowed, or the
- * forward stopped at T == weight_threshold exactly (the backward's stop rule
- * is T < weight_threshold).  Given the same record, the backward enters the
- * recorded cells of the other rays without scanning their faces, and walks
- * the flagged ones in a second launch, with results identical to a backward
- * without the record.  The record is only valid for the scene,
- * rays, start cells and max_intersections of the forward that wrote it.  No
- * reference counterpart (the reference's backward re-walks every ray). */
+/* Path record: the training forward stores, for each ray and walk step, the
+ * cell it enters and the colour it computed for the segment integrated at
+ * that step: steps (cap, num_rays) records of 16 bytes {u32 cell, f32 r, g,
+ * b} (0 colour for untextured cells and empty segments), slot-major:
+ * steps[k * num_rays + r], 16-byte aligned; len (num_rays) u32 = the number
+ * of steps that found an exit face (steps beyond cap are not stored).  Bit 31
+ * of len flags a ray that the backward must walk itself: the record
+ * overflowed, or the forward stopped at T == weight_threshold exactly (the
+ * backward's stop rule is T < weight_threshold).  Given the same record, the
+ * backward enters the recorded cells of the other rays without scanning their
+ * faces and without re-reading their texels, and walks the flagged ones in a
+ * second launch (replaying their stored prefix first), with results identical
+ * to a backward without the record.  The record is only valid for the inputs
+ * of the forward that wrote it.  No reference counterpart (the reference's
+ * backward re-walks every ray). */
 typedef struct {
-    uint32_t *cells;
+    void *steps;
     uint32_t cap;
     uint32_t *len;
 } vt_path;

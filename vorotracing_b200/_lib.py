@@ -21,7 +21,7 @@ class VtScene(C.Structure):
 
 
 class VtPath(C.Structure):
-    _fields_ = [("cells", C.c_void_p), ("cap", C.c_uint32), ("len", C.c_void_p)]
+    _fields_ = [("steps", C.c_void_p), ("cap", C.c_uint32), ("len", C.c_void_p)]
 
 
 class VtDebug(C.Structure):

@@ -45,8 +45,12 @@ template <class AT> struct FwdOut {
     PathRec rec;
 };
 
-template <class AT, int R, bool kDebug>
-__global__ void __launch_bounds__(kTrainBlock, VT_FWD_MIN_BLOCKS)
+#ifndef VT_FWD_REC_MIN_BLOCKS
+#define VT_FWD_REC_MIN_BLOCKS 7  // the record store needs a few more registers
+#endif
+
+template <class AT, int R, bool kDebug, bool kRec>
+__global__ void __launch_bounds__(kTrainBlock, kRec ? VT_FWD_REC_MIN_BLOCKS : VT_FWD_MIN_BLOCKS)
     fwd_kernel(TrainCommon a, TexPlain<AT, R> tex, FwdOut<AT> o)
 {
     uint32_t r = blockIdx.x * blockDim.x + threadIdx.x;
@@ -60,15 +64,12 @@ __global__ void __launch_bounds__(kTrainBlock, VT_FWD_MIN_BLOCKS)
     uint32_t n = 0;
     if (start >= a.n_points) {
         report(a.err, VT_ERR_DATA);
-        if (o.rec.cells) o.rec.len[r] = kPathWalk;
-    } else if (o.rec.cells) {
-        n = walk<FwdInteg<AT, R>, kDebug, true>(ray, a.faces, a.offs, a.points, a.density, start,
-                                                a.max_steps, I, r, o.dbg, o.rec);
+        if (kRec) o.rec.len[r] = kPathWalk;
     } else {
-        n = walk<FwdInteg<AT, R>, kDebug>(ray, a.faces, a.offs, a.points, a.density, start,
-                                          a.max_steps, I, r, o.dbg);
+        n = walk<FwdInteg<AT, R>, kDebug, kRec>(ray, a.faces, a.offs, a.points, a.density, start,
+                                                a.max_steps, I, r, o.dbg, o.rec);
     }
-    if (o.rec.cells && (o.rec.len[r] > o.rec.cap || I.T == a.wt)) o.rec.len[r] |= kPathWalk;
+    if (kRec && (o.rec.len[r] > o.rec.cap || I.T == a.wt)) o.rec.len[r] |= kPathWalk;
     for (uint32_t i = I.qi; i < a.K; ++i) {
         qd[i] = -1.0f;
         qi[i] = 0xffffffffu;
@@ -177,13 +178,13 @@ __global__ void __launch_bounds__(kTrainBlock, VT_BWD_MIN_BLOCKS)
     if (M == kBwdReplay) {
         WalkState w;
         walk_replay<BwdInteg<AT, R, F>>(ray, a.points, a.density, start, min(L, a.max_steps), I,
-                                        b.rec.cells + r, b.rec.stride, w);
+                                        b.rec.steps + r, b.rec.stride, w);
     } else if (M == kBwdWalkFlagged) {
         // replay what the record holds, then walk on with the face scan
         WalkState w;
         const uint32_t Lr = min(min(L & ~kPathWalk, b.rec.cap), a.max_steps);
         if (walk_replay<BwdInteg<AT, R, F>>(ray, a.points, a.density, start, Lr, I,
-                                            b.rec.cells + r, b.rec.stride, w)) {
+                                            b.rec.steps + r, b.rec.stride, w)) {
             w.begin = __ldg(a.offs + w.cur);
             w.deg = __ldg(a.offs + w.cur + 1) - w.begin;
             WalkDebug none{nullptr, 0, nullptr, nullptr, nullptr, nullptr};
@@ -236,9 +237,11 @@ vt_status launch_fwd(const TrainCommon &a, const void *dif, const void *spe, con
     TexPlain<AT, R> t{(const AT *)dif, (const AT *)spe};
     unsigned g = grid_for(a.num_rays, kTrainBlock);
     if (debug)
-        fwd_kernel<AT, R, true><<<g, kTrainBlock, 0, s>>>(a, t, o);
+        o.rec.steps ? fwd_kernel<AT, R, true, true><<<g, kTrainBlock, 0, s>>>(a, t, o)
+                    : fwd_kernel<AT, R, true, false><<<g, kTrainBlock, 0, s>>>(a, t, o);
     else
-        fwd_kernel<AT, R, false><<<g, kTrainBlock, 0, s>>>(a, t, o);
+        o.rec.steps ? fwd_kernel<AT, R, false, true><<<g, kTrainBlock, 0, s>>>(a, t, o)
+                    : fwd_kernel<AT, R, false, false><<<g, kTrainBlock, 0, s>>>(a, t, o);
     return check_launch("fwd_kernel");
 }
 
@@ -264,7 +267,7 @@ vt_status launch_bwd(const TrainCommon &a, const void *dif, const void *spe, Bwd
     switch (F) {
 #define VT_BWD_CASE(f)                                                                             \
     case f:                                                                                        \
-        if (b.rec.cells) {                                                                         \
+        if (b.rec.steps) {                                                                         \
             bwd_kernel<AT, R, f, kBwdReplay><<<g, kTrainBlock, 0, s>>>(a, t, b);                   \
             bwd_kernel<AT, R, f, kBwdWalkFlagged><<<g, kTrainBlock, 0, s>>>(a, t, b);              \
         } else {                                                                                   \
@@ -312,9 +315,10 @@ extern "C" vt_status vt_trace_fwd(const vt_scene *scene, int attr_half, const vo
         dbg = vt::WalkDebug{debug->seq, debug->seq_cap, debug->seq_len, (uint4 *)debug->stats,
                             debug->visited, debug->textured};
     vt::PathRec rec{nullptr, 0, 0, nullptr};
-    if (path && path->cells && path->cap) {
+    if (path && path->steps && path->cap) {
         VT_REQUIRE(path->len, "vt_trace_fwd: path record without len");
-        rec = vt::PathRec{path->cells, path->cap, num_rays, path->len};
+        VT_REQUIRE(((uintptr_t)path->steps & 15u) == 0, "vt_trace_fwd: path steps must be 16-byte aligned");
+        rec = vt::PathRec{(uint4 *)path->steps, path->cap, num_rays, path->len};
     }
     cudaStream_t s = (cudaStream_t)stream;
     if (attr_half) {
@@ -369,9 +373,10 @@ extern "C" vt_status vt_trace_bwd(const vt_scene *scene, int attr_half, const vo
                "vt_trace_bwd: depth_grad must be provided if depth_quantiles is provided");
     if (num_rays == 0) return VT_OK;
     vt::PathRec rec{nullptr, 0, 0, nullptr};
-    if (path && path->cells && path->cap) {
+    if (path && path->steps && path->cap) {
         VT_REQUIRE(path->len, "vt_trace_bwd: path record without len");
-        rec = vt::PathRec{path->cells, path->cap, num_rays, path->len};
+        VT_REQUIRE(((uintptr_t)path->steps & 15u) == 0, "vt_trace_bwd: path steps must be 16-byte aligned");
+        rec = vt::PathRec{(uint4 *)path->steps, path->cap, num_rays, path->len};
     }
     cudaStream_t s = (cudaStream_t)stream;
     if (attr_half) {

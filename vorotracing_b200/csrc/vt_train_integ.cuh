@@ -71,6 +71,7 @@ template <class AT, int R> struct FwdInteg {
     float W, S, dist, self, tfar;
     float s_prev;  // 1 - 1/(1 + t0) of the current t0 (the previous segment's s1)
     AT *contrib;
+    V3 last_rgb;   // colour of the last integrated segment (for the path record)
 
     __device__ __forceinline__ FwdInteg(const Ray &r, const TexPlain<AT, R> &t, float wt_,
                                         const float *qthr_, uint32_t K_, float *qdepth_,
@@ -98,6 +99,7 @@ template <class AT, int R> struct FwdInteg {
             rgb = mk(sigmoid(l.x), sigmoid(l.y), sigmoid(l.z));
             ntex++;
         }
+        last_rgb = rgb;
         float delta = fmaxf(t1 - t0, 0.0f);
         float alpha = 1.0f - expf_exact(-s * delta);
         float w = T * alpha;
@@ -213,6 +215,22 @@ template <class AT, int R, int F = kBwdDepth | kBwdDist | kBwdErr> struct BwdInt
 
     __device__ __forceinline__ bool integrate(uint32_t cell, float t0, float t1, V3 P, V3 Q, float s)
     {
+        return integrate_impl<false>(cell, t0, t1, P, Q, s, mk(0.f, 0.f, 0.f));
+    }
+
+    // The same with the segment's colour taken from the forward's path
+    // record instead of re-sampling the texels (the forward computed it with
+    // this very arithmetic, so the values are identical).
+    __device__ __forceinline__ bool integrate_recorded(uint32_t cell, float t0, float t1, V3 P,
+                                                       V3 Q, float s, V3 rgb_fwd)
+    {
+        return integrate_impl<true>(cell, t0, t1, P, Q, s, rgb_fwd);
+    }
+
+    template <bool kRecorded>
+    __device__ __forceinline__ bool integrate_impl(uint32_t cell, float t0, float t1, V3 P, V3 Q,
+                                                   float s, V3 rgb_fwd)
+    {
         V3 rgb = mk(0.f, 0.f, 0.f);
         Bilin db;
         bool has_color = false;
@@ -220,8 +238,12 @@ template <class AT, int R, int F = kBwdDepth | kBwdDist | kBwdErr> struct BwdInt
             float tu, tv;
             oct_encode<R>(probe_dir(ray, t0, P), tu, tv);
             db = make_bilin<R>(tu, tv);
-            V3 l = tex.logits(cell, db, spec);
-            rgb = mk(sigmoid(l.x), sigmoid(l.y), sigmoid(l.z));
+            if (kRecorded) {
+                rgb = rgb_fwd;
+            } else {
+                V3 l = tex.logits(cell, db, spec);
+                rgb = mk(sigmoid(l.x), sigmoid(l.y), sigmoid(l.z));
+            }
             has_color = true;
             ntex++;
         }

@@ -77,12 +77,14 @@ __device__ __forceinline__ void test_chunk_idx(const FaceChunk &c, uint32_t j, u
 
 // Path record of the training forward, replayed by the backward.  Slot k of
 // ray r holds the cell entered at walk step k (the exit neighbour found at
-// step k), laid out slot-major (cells[k * stride + r]) so that the lanes of a
-// warp, which advance one cell per loop iteration together, touch
-// consecutive words.  len[r] = number of exit faces found (steps past cap are
-// not stored; the replay then resumes the face scan where the record ends).
+// step k) and the colour the forward computed for the segment integrated at
+// step k (sigmoid of the sampled logits; 0 when the cell is untextured or the
+// segment is empty): {cell, r, g, b bits} in 16 bytes, laid out slot-major
+// (steps[k * stride + r]) so that the lanes of a warp, which advance one cell
+// per loop iteration together, touch consecutive records.  len[r] = number
+// of exit faces found (steps past cap are not stored).
 struct PathRec {
-    uint32_t *cells;
+    uint4 *steps;
     uint32_t cap;
     uint64_t stride;
     uint32_t *len;
@@ -159,21 +161,27 @@ __device__ __forceinline__ uint32_t walk_from(WalkState w, const Ray &ray,
         }
 
         if (!x.found) break;
-        if (kRecord) {
-            if (nfound < rec.cap) rec.cells[(uint64_t)nfound * rec.stride + ray_id] = x.nb;
-            nfound++;
-        }
         // Issue the next cell's loads before integrating this one.
         V3 Q = ld3(points + (size_t)x.nb * 3);
         float sn = __ldg(density + x.nb);
         load_chunk(c, faces + x.nbeg, 0, x.ndeg);
+        bool go = true;
+        V3 rgb = mk(0.f, 0.f, 0.f);
         if (x.t1 > t0) {
             if (kDebug) nint++;
             const uint32_t tex_before = kDebug ? I.textured() : 0;
-            const bool go = I.integrate(cur, t0, x.t1, P, Q, s);
+            go = I.integrate(cur, t0, x.t1, P, Q, s);
+            if constexpr (kRecord) rgb = I.last_rgb;
             if (kDebug && dbg.textured && I.textured() != tex_before) dbg.textured[cur] = 1;
-            if (!go) break;
         }
+        if (kRecord) {
+            if (nfound < rec.cap)
+                rec.steps[(uint64_t)nfound * rec.stride + ray_id] =
+                    make_uint4(x.nb, __float_as_uint(rgb.x), __float_as_uint(rgb.y),
+                               __float_as_uint(rgb.z));
+            nfound++;
+        }
+        if (!go) break;
         t0 = fmaxf(t0, x.t1);
         cur = x.nb;
         P = Q;
@@ -217,7 +225,8 @@ constexpr uint32_t kPathWalk = 0x80000000u;
 
 // Backward replay: the cells of the forward's path record are entered
 // without scanning faces (the exit distance is recomputed from the two
-// sites).  The walk is deterministic, so every recorded step is the step the
+// sites), and each segment's colour is the forward's, so no texel is read
+// back (Integ::integrate_recorded).  The walk is deterministic, so every recorded step is the step the
 // scan would take, and an unflagged record ends where the backward's walk
 // ends (no exit face, the step limit, or T < weight_threshold, which stopped
 // the forward at the same step).  Returns false if the integrator stopped the
@@ -228,41 +237,44 @@ constexpr uint32_t kPathWalk = 0x80000000u;
 template <class Integ>
 __device__ __forceinline__ bool walk_replay(const Ray &ray, const float *__restrict__ points,
                                             const float *__restrict__ density, uint32_t start,
-                                            uint32_t L, Integ &I, const uint32_t *cells,
+                                            uint32_t L, Integ &I, const uint4 *steps,
                                             uint64_t stride, WalkState &w)
 {
     uint32_t cur = start;
     V3 P = ld3(points + (size_t)start * 3);
     float s = __ldg(density + start);
     float t0 = 0.0f;
-    uint32_t nb = 0, nb1 = 0;
+    uint4 st = make_uint4(0, 0, 0, 0), st1 = make_uint4(0, 0, 0, 0);
     V3 Q = P;
     float sq = 0.0f;
     if (L > 0) {
-        nb = __ldg(cells);
-        Q = ld3(points + (size_t)nb * 3);
-        sq = __ldg(density + nb);
+        st = __ldg(steps);
+        Q = ld3(points + (size_t)st.x * 3);
+        sq = __ldg(density + st.x);
     }
-    if (L > 1) nb1 = __ldg(cells + stride);
+    if (L > 1) st1 = __ldg(steps + stride);
     for (uint32_t k = 0; k < L; ++k) {
         V3 Qn = Q;
         float sqn = 0.0f;
-        uint32_t nb2 = 0;
+        uint4 st2 = make_uint4(0, 0, 0, 0);
         if (k + 1 < L) {
-            Qn = ld3(points + (size_t)nb1 * 3);
-            sqn = __ldg(density + nb1);
+            Qn = ld3(points + (size_t)st1.x * 3);
+            sqn = __ldg(density + st1.x);
         }
-        if (k + 2 < L) nb2 = __ldg(cells + (uint64_t)(k + 2) * stride);
+        if (k + 2 < L) st2 = __ldg(steps + (uint64_t)(k + 2) * stride);
         const float t1 = face_exit_t(P, Q, ray);
-        if (t1 > t0 && !I.integrate(cur, t0, t1, P, Q, s)) return false;
+        if (t1 > t0) {
+            const V3 rgb = mk(__uint_as_float(st.y), __uint_as_float(st.z), __uint_as_float(st.w));
+            if (!I.integrate_recorded(cur, t0, t1, P, Q, s, rgb)) return false;
+        }
         t0 = fmaxf(t0, t1);
-        cur = nb;
+        cur = st.x;
         P = Q;
         s = sq;
-        nb = nb1;
+        st = st1;
         Q = Qn;
         sq = sqn;
-        nb1 = nb2;
+        st1 = st2;
     }
     w.cur = cur;
     w.P = P;

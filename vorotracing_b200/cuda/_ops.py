@@ -453,22 +453,33 @@ def _train_checks(points, diffuse, specular, density, adjacency, offsets, rays, 
 
 
 class PathRecord:
-    """Per-ray cell sequence written by the training forward and replayed by
-    the backward (vt_path): ``cells`` (cap, num_rays) uint32 slot-major,
-    ``len`` (num_rays,) uint32.  cap * num_rays * 4 bytes of device memory;
-    rays longer than ``cap`` steps resume the face scan after the stored
-    prefix."""
+    """Per-ray walk record written by the training forward and replayed by
+    the backward (vt_path): ``steps`` (cap, num_rays, 4) 32-bit words per
+    step {cell id, r, g, b as float32 bits}, slot-major; ``len`` (num_rays,)
+    uint32 (bit 31: the backward walks the ray itself).  cap * num_rays * 16
+    bytes of device memory; rays longer than ``cap`` steps resume the face
+    scan after the stored prefix."""
 
     def __init__(self, num_rays: int, cap: int, device):
         self.cap = int(cap)
         self.num_rays = int(num_rays)
-        self.cells = torch.empty((self.cap, self.num_rays), dtype=torch.uint32, device=device)
+        self.steps = torch.empty((self.cap, self.num_rays, 4), dtype=torch.int32, device=device)
         self.len = torch.empty(self.num_rays, dtype=torch.uint32, device=device)
+
+    @property
+    def cells(self) -> torch.Tensor:
+        """(cap, num_rays) uint32 cell entered at each step."""
+        return self.steps[..., 0].view(torch.uint32)
+
+    @property
+    def colors(self) -> torch.Tensor:
+        """(cap, num_rays, 3) float32 colour of the segment integrated at each step."""
+        return self.steps[..., 1:].view(torch.float32)
 
     def struct(self, nr: int):
         if nr != self.num_rays:
             _fail("path record was made for a different number of rays")
-        return _lib.VtPath(self.cells.data_ptr(), self.cap, self.len.data_ptr())
+        return _lib.VtPath(self.steps.data_ptr(), self.cap, self.len.data_ptr())
 
 
 def _path_arg(path, nr):

@@ -28,10 +28,11 @@ class TraceVoroTracing(torch.autograd.Function):
     face rows built in forward are reused by backward (the sites cannot change
     in between), where the reference rebuilds its adj_diff on every call.
 
-    The forward also records each ray's first ``path_cap`` cells
-    (``path_cap`` * 4 bytes per ray, held until backward) so that the
-    backward enters them without scanning faces; set ``path_cap = 0`` to
-    re-walk instead.  Gradients are the same either way."""
+    The forward also records each ray's first ``path_cap`` steps (cell and
+    segment colour, ``path_cap`` * 16 bytes per ray, held until backward) so
+    that the backward enters them without scanning faces or re-reading
+    texels; set ``path_cap = 0`` to re-walk instead.  Gradients are the same
+    either way."""
 
     path_cap = 256
 
