@@ -156,11 +156,10 @@ def run_c4(args, ws, rank, dev):
             start, None, WT, 1024, False, faces=faces, path=path)
         g = torch.zeros_like(rgba)
         g[:, :3] = (2.0 / (nr * 3)) * (rgba[:, :3] - target)
-        bucket.zero_()
         _ops.trace_vorotracing_bwd(t["points"], t["diffuse"], t["specular"], t["density"],
                                    t["adj"], t["offs"], rays, start, rgba, g, None, None, None,
                                    None, 0.0, dist_, None, Wt, St, tfar, WT, 1024, faces=faces,
-                                   grads=bucket.views(), path=path)
+                                   grads=bucket.views(), path=path, accumulate=False)
         bucket.allreduce_()
 
     if args.profile:

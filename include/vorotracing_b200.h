@@ -169,8 +169,8 @@ VT_API vt_status vt_trace_fwd(const vt_scene *scene, int attr_half, const void *
                               float *S_total, float *t_far, const vt_debug *debug,
                               const vt_path *path, uint32_t *err, vt_stream stream);
 
-/* Training backward.  Gradient outputs must be zero-initialised by the
- * caller: points_grad (N,3) f32, diffuse/specular_grad in the attribute
+/* Training backward.  Gradients are added to the outputs (zero-initialised
+ * by the caller), or overwrite them with VT_BWD_OVERWRITE: points_grad (N,3) f32, diffuse/specular_grad in the attribute
  * dtype, density_grad (N) f32, point_error (N) attribute dtype or null
  * (accumulated only when ray_error is given).  path: null (walk every ray),
  * or the record written by the matching forward. */
@@ -185,7 +185,11 @@ VT_API vt_status vt_trace_bwd(const vt_scene *scene, int attr_half, const void *
                               uint32_t max_intersections, float *points_grad, void *diffuse_grad,
                               void *specular_grad, float *density_grad, void *point_error,
                               void *workspace, uint64_t workspace_bytes, const vt_path *path,
-                              uint32_t *err, vt_stream stream);
+                              uint32_t flags, uint32_t *err, vt_stream stream);
+/* vt_trace_bwd flags.  VT_BWD_OVERWRITE: the gradient outputs are
+ * overwritten instead of accumulated into, so they need no zero
+ * initialisation (requires the workspace). */
+#define VT_BWD_OVERWRITE 1u
 /* Optional scratch of vt_trace_bwd (256-byte aligned): with it the texel and
  * site gradients accumulate in padded fp32 rows with one vector atomic per
  * texel (instead of three scalar atomics) and are added to the outputs at the

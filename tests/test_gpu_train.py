@@ -207,6 +207,20 @@ def test_bwd_into_flat_bucket(c1_scene, c1_rays):
     for got, want in zip(b.views(), (ref[0], ref[1], ref[2], ref[3])):
         scale = float(want.abs().max()) if want.numel() else 1.0
         torch.testing.assert_close(got.reshape(want.shape), want, rtol=1e-4, atol=1e-5 * scale)
+    # overwrite mode: the bucket's previous contents do not matter
+    b.flat.fill_(123.0)
+    _ops.trace_vorotracing_bwd(*args, *common, grads=b.views(), accumulate=False)
+    for got, want in zip(b.views(), (ref[0], ref[1], ref[2], ref[3])):
+        scale = float(want.abs().max()) if want.numel() else 1.0
+        torch.testing.assert_close(got.reshape(want.shape), want, rtol=1e-4, atol=1e-5 * scale)
+    # no rays: overwriting leaves zero gradients
+    b.flat.fill_(123.0)
+    empty = lambda t: t[:0]
+    _ops.trace_vorotracing_bwd(*args[:6], empty(args[6]), empty(args[7]), empty(f[0]),
+                               empty(gr), None, None, None, None, 0.0, empty(f[5]), None,
+                               empty(f[6]), empty(f[7]), empty(f[8]), 0.01, 1024,
+                               grads=b.views(), accumulate=False)
+    assert not b.flat.any()
 
 
 @pytest.mark.parametrize("half", [False, True])

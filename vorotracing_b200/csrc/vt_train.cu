@@ -199,17 +199,23 @@ __global__ void __launch_bounds__(kTrainBlock, VT_BWD_MIN_BLOCKS)
     }
 }
 
-// out[t*3 + c] += scratch[t].c for every texel (or site) t.
-template <class AT>
+// out[t*3 + c] += scratch[t].c for every texel (or site) t; kSet: = instead.
+template <class AT, bool kSet>
 __global__ void compact4_kernel(const float4 *__restrict__ scratch, uint64_t n, AT *__restrict__ out)
 {
     uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (t >= n) return;
     float4 v = scratch[t];
     AT *o = out + t * 3;
-    o[0] = fromf<AT>(tof<AT>(o[0]) + v.x);
-    o[1] = fromf<AT>(tof<AT>(o[1]) + v.y);
-    o[2] = fromf<AT>(tof<AT>(o[2]) + v.z);
+    if (kSet) {
+        o[0] = fromf<AT>(v.x);
+        o[1] = fromf<AT>(v.y);
+        o[2] = fromf<AT>(v.z);
+    } else {
+        o[0] = fromf<AT>(tof<AT>(o[0]) + v.x);
+        o[1] = fromf<AT>(tof<AT>(o[1]) + v.y);
+        o[2] = fromf<AT>(tof<AT>(o[2]) + v.z);
+    }
 }
 
 inline size_t a256(size_t x) { return (x + 255) & ~(size_t)255; }
@@ -247,7 +253,7 @@ vt_status launch_fwd(const TrainCommon &a, const void *dif, const void *spe, con
 
 template <class AT, int R>
 vt_status launch_bwd(const TrainCommon &a, const void *dif, const void *spe, BwdIn<AT> b,
-                     void *ws, cudaStream_t s)
+                     void *ws, bool overwrite, cudaStream_t s)
 {
     TexPlain<AT, R> t{(const AT *)dif, (const AT *)spe};
     const uint64_t ntex = (uint64_t)a.n_points * R * R;
@@ -257,6 +263,10 @@ vt_status launch_bwd(const TrainCommon &a, const void *dif, const void *spe, Bwd
         b.sspec = (float4 *)(w + a256(ntex * 16));
         b.spts = (float4 *)(w + 2 * a256(ntex * 16));
         cudaError_t e = cudaMemsetAsync(ws, 0, 2 * a256(ntex * 16) + a256((size_t)a.n_points * 16), s);
+        if (e == cudaSuccess && overwrite)  // the outputs the kernels add to directly
+            e = cudaMemsetAsync(b.density_grad, 0, (size_t)a.n_points * 4, s);
+        if (e == cudaSuccess && overwrite && b.point_error)
+            e = cudaMemsetAsync(b.point_error, 0, (size_t)a.n_points * sizeof(AT), s);
         if (e != cudaSuccess) return set_error(VT_ERR_CUDA, "vt_trace_bwd memset: %s", cudaGetErrorString(e));
     } else {
         b.sdiff = b.sspec = b.spts = nullptr;
@@ -278,11 +288,16 @@ vt_status launch_bwd(const TrainCommon &a, const void *dif, const void *spe, Bwd
         VT_BWD_CASE(4) VT_BWD_CASE(5) VT_BWD_CASE(6) VT_BWD_CASE(7)
 #undef VT_BWD_CASE
     }
-    if (ws) {
-        compact4_kernel<AT><<<grid_for(ntex, 256), 256, 0, s>>>(b.sdiff, ntex, b.diffuse_grad);
-        compact4_kernel<AT><<<grid_for(ntex, 256), 256, 0, s>>>(b.sspec, ntex, b.specular_grad);
-        compact4_kernel<float><<<grid_for(a.n_points, 256), 256, 0, s>>>(b.spts, a.n_points,
-                                                                          b.points_grad);
+    if (ws && overwrite) {
+        compact4_kernel<AT, true><<<grid_for(ntex, 256), 256, 0, s>>>(b.sdiff, ntex, b.diffuse_grad);
+        compact4_kernel<AT, true><<<grid_for(ntex, 256), 256, 0, s>>>(b.sspec, ntex, b.specular_grad);
+        compact4_kernel<float, true><<<grid_for(a.n_points, 256), 256, 0, s>>>(b.spts, a.n_points,
+                                                                                b.points_grad);
+    } else if (ws) {
+        compact4_kernel<AT, false><<<grid_for(ntex, 256), 256, 0, s>>>(b.sdiff, ntex, b.diffuse_grad);
+        compact4_kernel<AT, false><<<grid_for(ntex, 256), 256, 0, s>>>(b.sspec, ntex, b.specular_grad);
+        compact4_kernel<float, false><<<grid_for(a.n_points, 256), 256, 0, s>>>(b.spts, a.n_points,
+                                                                                 b.points_grad);
     }
     return check_launch("bwd_kernel");
 }
@@ -353,8 +368,8 @@ extern "C" vt_status vt_trace_bwd(const vt_scene *scene, int attr_half, const vo
                                   float weight_threshold, uint32_t max_intersections,
                                   float *points_grad, void *diffuse_grad, void *specular_grad,
                                   float *density_grad, void *point_error, void *workspace,
-                                  uint64_t workspace_bytes, const vt_path *path, uint32_t *err,
-                                  vt_stream stream)
+                                  uint64_t workspace_bytes, const vt_path *path, uint32_t flags,
+                                  uint32_t *err, vt_stream stream)
 {
     vt::TrainCommon a;
     vt_status st = vt::fill_common(a, scene, rays, num_rays, start, num_quantiles, depth_quantiles,
@@ -364,6 +379,9 @@ extern "C" vt_status vt_trace_bwd(const vt_scene *scene, int attr_half, const vo
     VT_REQUIRE(!workspace || (((uintptr_t)workspace & 255u) == 0 &&
                               workspace_bytes >= vt_trace_bwd_workspace_bytes(scene->num_points, res)),
                "vt_trace_bwd: workspace must be 256-byte aligned and vt_trace_bwd_workspace_bytes large");
+    VT_REQUIRE(!(flags & VT_BWD_OVERWRITE) || workspace,
+               "vt_trace_bwd: VT_BWD_OVERWRITE needs the workspace");
+    const bool overwrite = (flags & VT_BWD_OVERWRITE) != 0;
     if (st != VT_OK) return st;
     VT_REQUIRE(diffuse && specular, "vt_trace_bwd: null textures");
     VT_REQUIRE(num_rays == 0 || (rgba && rgba_grad), "vt_trace_bwd: null rgba inputs");
@@ -371,7 +389,19 @@ extern "C" vt_status vt_trace_bwd(const vt_scene *scene, int attr_half, const vo
                "vt_trace_bwd: null gradient outputs");
     VT_REQUIRE(num_quantiles == 0 || (quantile_indices && depth_grad),
                "vt_trace_bwd: depth_grad must be provided if depth_quantiles is provided");
-    if (num_rays == 0) return VT_OK;
+    if (num_rays == 0) {
+        if (!overwrite) return VT_OK;
+        // nothing to add: overwriting means zero gradients
+        const size_t n = scene->num_points, at = attr_half ? 2 : 4;
+        cudaStream_t s0 = (cudaStream_t)stream;
+        cudaError_t e = cudaMemsetAsync(points_grad, 0, n * 12, s0);
+        if (e == cudaSuccess) e = cudaMemsetAsync(diffuse_grad, 0, n * 3 * res * res * at, s0);
+        if (e == cudaSuccess) e = cudaMemsetAsync(specular_grad, 0, n * 3 * res * res * at, s0);
+        if (e == cudaSuccess) e = cudaMemsetAsync(density_grad, 0, n * 4, s0);
+        if (e == cudaSuccess && point_error) e = cudaMemsetAsync(point_error, 0, n * at, s0);
+        if (e != cudaSuccess) return vt::set_error(VT_ERR_CUDA, "vt_trace_bwd: %s", cudaGetErrorString(e));
+        return VT_OK;
+    }
     vt::PathRec rec{nullptr, 0, 0, nullptr};
     if (path && path->steps && path->cap) {
         VT_REQUIRE(path->len, "vt_trace_bwd: path record without len");
@@ -386,8 +416,8 @@ extern "C" vt_status vt_trace_bwd(const vt_scene *scene, int attr_half, const vo
                             (__half *)diffuse_grad, (__half *)specular_grad, density_grad,
                             (__half *)point_error};
         b.rec = rec;
-        if (res == 8) return vt::launch_bwd<__half, 8>(a, diffuse, specular, b, workspace, s);
-        if (res == 4) return vt::launch_bwd<__half, 4>(a, diffuse, specular, b, workspace, s);
+        if (res == 8) return vt::launch_bwd<__half, 8>(a, diffuse, specular, b, workspace, overwrite, s);
+        if (res == 4) return vt::launch_bwd<__half, 4>(a, diffuse, specular, b, workspace, overwrite, s);
     } else {
         vt::BwdIn<float> b{quantile_indices, (const float *)rgba, (const float *)rgba_grad,
                            depth_grad, (const float *)ray_error, contribution_alpha_grad,
@@ -395,8 +425,8 @@ extern "C" vt_status vt_trace_bwd(const vt_scene *scene, int attr_half, const vo
                            (float *)diffuse_grad, (float *)specular_grad, density_grad,
                            (float *)point_error};
         b.rec = rec;
-        if (res == 8) return vt::launch_bwd<float, 8>(a, diffuse, specular, b, workspace, s);
-        if (res == 4) return vt::launch_bwd<float, 4>(a, diffuse, specular, b, workspace, s);
+        if (res == 8) return vt::launch_bwd<float, 8>(a, diffuse, specular, b, workspace, overwrite, s);
+        if (res == 4) return vt::launch_bwd<float, 4>(a, diffuse, specular, b, workspace, overwrite, s);
     }
     return vt::set_error(VT_ERR_INVALID, "vt_trace_bwd: res must be 4 or 8, got %d", res);
 }

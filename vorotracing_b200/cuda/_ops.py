@@ -548,10 +548,12 @@ def trace_vorotracing_bwd(points, diffuse, specular, density, adjacency, offsets
                           depth_grad, ray_error, contribution_alpha_grad: float, distortion,
                           distortion_grad, W_total, S_total, t_far, weight_threshold: float,
                           max_intersections: int, faces=None, grads=None,
-                          vector_atomics: bool = True, path: PathRecord | None = None):
+                          vector_atomics: bool = True, path: PathRecord | None = None,
+                          accumulate: bool = True):
     """Training backward (tracing_octmap.cu:860-1103).  Gradients go to new
-    zeroed tensors, or accumulate into ``grads`` = (points, diffuse, specular,
-    density) when given.  Returns the reference's 6-tuple (points_grad, diffuse_grad, specular_grad, density_grad, ray_grad,
+    tensors, or into ``grads`` = (points, diffuse, specular, density) when
+    given: added to them, or (``accumulate=False``) overwriting them, which
+    spares the caller zeroing them.  Returns the reference's 6-tuple (points_grad, diffuse_grad, specular_grad, density_grad, ray_grad,
     point_error); ray_grad is allocated and never written, as in the
     reference; point_error is None unless ray_error is given.  ``path``: the
     PathRecord filled by the forward of the same inputs (the walk then skips
@@ -598,13 +600,15 @@ def trace_vorotracing_bwd(points, diffuse, specular, density, adjacency, offsets
             _fail("depth_grad must have the same batch size as rays")
     perr = re = None
     n = points.size(0)
+    # the kernels overwrite the outputs when they accumulate in the workspace
+    overwrite = bool(vector_atomics) and (grads is None or not accumulate)
     if ray_error is not None:
         re = ray_error.contiguous()
         if re.dtype != diffuse.dtype:
             _fail("ray_error must have the same dtype as diffuse/specular")
         if re.numel() != nr:
             _fail("ray_error must have the same batch size as rays")
-        perr = torch.zeros((n, 1), dtype=diffuse.dtype, device=dev)
+        perr = (torch.empty if overwrite else torch.zeros)((n, 1), dtype=diffuse.dtype, device=dev)
     ts = {}
     for name, t in (("W_total", W_total), ("S_total", S_total), ("t_far", t_far),
                     ("distortion", distortion)):
@@ -622,13 +626,17 @@ def trace_vorotracing_bwd(points, diffuse, specular, density, adjacency, offsets
         if dgr.numel() != nr:
             _fail("distortion_grad must have the same batch size as rays")
     if grads is None:
-        diffuse_grad = torch.zeros_like(diffuse)
-        specular_grad = torch.zeros_like(specular)
-        density_grad = torch.zeros_like(density, dtype=torch.float32)
-        points_grad = torch.zeros((n, 3), dtype=torch.float32, device=dev)
+        alloc = torch.empty_like if overwrite else torch.zeros_like
+        diffuse_grad = alloc(diffuse)
+        specular_grad = alloc(specular)
+        density_grad = alloc(density, dtype=torch.float32)
+        points_grad = alloc(points, dtype=torch.float32).reshape(n, 3)
     else:
-        # caller-provided, zero-initialised (e.g. views of a flat all-reduce bucket)
+        # caller-provided (e.g. views of a flat all-reduce bucket)
         points_grad, diffuse_grad, specular_grad, density_grad = grads
+        if not accumulate and not overwrite:
+            for t in grads:
+                t.zero_()
         if (points_grad.shape != (n, 3) or points_grad.dtype != torch.float32
                 or diffuse_grad.shape != diffuse.shape or diffuse_grad.dtype != diffuse.dtype
                 or specular_grad.shape != specular.shape
@@ -643,7 +651,7 @@ def trace_vorotracing_bwd(points, diffuse, specular, density, adjacency, offsets
     scene = make_scene(points, density, offsets, faces)
     err = torch.zeros(1, dtype=torch.int32, device=dev)
     ws, wsb = None, 0
-    if vector_atomics and nr:
+    if vector_atomics:
         wsb = int(lib().vt_trace_bwd_workspace_bytes(C.c_uint32(n), C.c_int(res)))
         ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
     check(lib().vt_trace_bwd(C.byref(scene), C.c_int(half), ptr(diffuse), ptr(specular),
@@ -654,7 +662,8 @@ def trace_vorotracing_bwd(points, diffuse, specular, density, adjacency, offsets
                              ptr(ts["S_total"]), C.c_float(weight_threshold),
                              C.c_uint32(max_intersections), ptr(points_grad), ptr(diffuse_grad),
                              ptr(specular_grad), ptr(density_grad), ptr(perr), ptr(ws),
-                             C.c_uint64(wsb), _path_arg(path, nr), ptr(err), stream_ptr(dev)),
+                             C.c_uint64(wsb), _path_arg(path, nr),
+                             C.c_uint32(1 if overwrite else 0), ptr(err), stream_ptr(dev)),
           "vt_trace_bwd")
     if _CHECK_ERRORS:
         _check_err(err)
