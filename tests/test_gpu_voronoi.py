@@ -26,7 +26,7 @@ def _compare(pts):
     rows, ref = _rows(offs, adj), _rows(ref_offs, ref_adj)
     # Cells of hull sites are unbounded and those of their Delaunay neighbours
     # can have faces far outside the scene; the GPU builder truncates cells to
-    # a box of 4x the scene extent, so those rows are left out of the row
+    # a box of 16x the scene extent, so those rows are left out of the row
     # comparison (the render test covers their effect on images).
     hull = set(ConvexHull(pts.astype(np.float64)).vertices.tolist())
     interior = [i for i in range(len(pts)) if i not in hull and not (ref[i] & hull)]

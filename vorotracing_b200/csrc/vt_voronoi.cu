@@ -4,7 +4,7 @@
 // (vorotracing/cuda/__init__.py:16-46, called every 1-100 training steps,
 // vorotracing/trainer.py:354-360).  Method: each site's Voronoi cell is built
 // independently by clipping (one thread per site):
-//   1. the cell starts as a box around the site (4x the scene extent) and is
+//   1. the cell starts as a box around the site (16x the scene extent) and is
 //      clipped by the bisector planes of the site's 24 nearest sites (exact
 //      k-NN from a uniform grid);
 //   2. every vertex v of the cell is then verified by the empty-ball
@@ -664,7 +664,11 @@ extern "C" vt_status vt_voronoi_adjacency(const float *points, uint32_t num_poin
     }
     g.lo = make_float3(bb[0], bb[2], bb[4]);
     g.inv_h = (float)(1.0 / h);
-    const float box = 4.0f * emax + 1.0f;
+#ifndef VT_VOR_BOX
+#define VT_VOR_BOX 16.0f  // truncation box half-width in scene extents (measured: 4 -> 16 cuts the
+                          // rows missing hull faces 5x for 40 % more build time)
+#endif
+    const float box = VT_VOR_BOX * emax + 1.0f;
     cudaMemsetAsync(v.cnt, 0, (G + 1) * 4, s);
     grid_count<<<vt::grid_for(n, 256), 256, 0, s>>>(points, n, g, v.cnt, v.cell_id);
     size_t tb = v.temp_bytes;
