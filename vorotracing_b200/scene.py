@@ -176,3 +176,36 @@ def config_rays(name: str, view: int = 0, n_views: int = 64) -> np.ndarray:
     else:
         T = orbit_pose(view, n_views)
     return pinhole_rays(intrinsics(W, H), T, W, H)
+
+
+def _main(argv=None):
+    """python -m vorotracing_b200.scene voronoi <config> [--sites N] [--repeat K]
+
+    Generates a configuration's sites and builds their Voronoi adjacency on
+    the GPU, printing the build time and entry count (a profiling target)."""
+    import argparse
+    import time
+
+    import torch
+
+    from .cuda import build_voronoi_adjacency
+
+    ap = argparse.ArgumentParser(prog="python -m vorotracing_b200.scene")
+    ap.add_argument("what", choices=["voronoi"])
+    ap.add_argument("config", choices=sorted(CONFIGS))
+    ap.add_argument("--sites", type=int, default=None)
+    ap.add_argument("--repeat", type=int, default=2)
+    a = ap.parse_args(argv)
+    c = CONFIGS[a.config]
+    pts = torch.from_numpy(make_sites(a.sites or c["n"], c["seed"], c["plane"])).cuda()
+    for _ in range(a.repeat):
+        torch.cuda.synchronize()
+        t = time.time()
+        adj, offs, status = build_voronoi_adjacency(pts)
+        torch.cuda.synchronize()
+        print(f"{a.config}: {pts.size(0)} sites, {int(offs[-1])} entries, "
+              f"{int(status[0])} unconverged, {time.time() - t:.3f} s", flush=True)
+
+
+if __name__ == "__main__":
+    _main()
