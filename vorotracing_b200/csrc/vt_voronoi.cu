@@ -3,10 +3,9 @@
 // The reference delegates this to the external `paragram` package
 // (vorotracing/cuda/__init__.py:16-46, called every 1-100 training steps,
 // vorotracing/trainer.py:354-360).  Method: each site's Voronoi cell is built
-// independently by clipping (one thread per site):
+// independently by clipping:
 //   1. the cell starts as a box around the site (16x the scene extent) and is
-//      clipped by the bisector planes of the site's 24 nearest sites (exact
-//      k-NN from a uniform grid);
+//      clipped by the bisector planes of nearby sites (seeds);
 //   2. every vertex v of the cell is then verified by the empty-ball
 //      property of Delaunay: no site may be closer to v than the cell's own
 //      site.  The ball B(v, |v - p_i|) is searched in a BVH of the sites; a
@@ -20,15 +19,19 @@
 // needles' vertex balls reach.  Cells of convex-hull sites are unbounded and
 // come out as their intersection with the box, so a face lying entirely
 // beyond the box is missing.
+// The first pass builds one cell per warp in shared memory
+// (vt_voronoi_warp.cuh); the cells it cannot finish are rebuilt here one per
+// thread (cell_verify_kernel: 48 exact nearest-site seeds, the cell in local
+// memory), then, if that fails too, by clipping with every site ring by ring
+// around the site (cell_stream_kernel, up to 16384).
 // The cell is stored in dual form: each vertex is a triangle of three plane
 // ids (counter-clockwise seen from outside) with its position and the three
 // neighbouring triangles across its edges.  A clip removes the triangles
 // whose vertex lies beyond the plane and closes the hole with a fan of new
 // triangles around the new plane.  Coordinates are relative to the site, so
 // bisector planes are n.x = |n|^2 / 2 with n = p_j - p_i.  Predicates are
-// binary32: a near-degenerate clip sequence can fail, and such cells are
-// rebuilt with 48 seed sites (another sequence), then, if that fails too,
-// by clipping with every site ring by ring around the site (up to 16384).
+// binary32, so a near-degenerate clip sequence can fail; the later passes
+// clip in another order.
 #include <cub/device/device_scan.cuh>
 
 #include "vt_abi.cuh"
@@ -495,6 +498,14 @@ __global__ void __launch_bounds__(64) cell_verify_kernel(
     count[i] = emit(C, nbr_out + (size_t)i * stride, stride);
 }
 
+}  // namespace vor
+}  // namespace vt
+
+#include "vt_voronoi_warp.cuh"
+
+namespace vt {
+namespace vor {
+
 // Final pass: clip against the sites ring by ring around the site's grid
 // cell until every site not yet scanned is farther than twice the farthest
 // cell vertex.  Convex-hull cells never get there (they reach the truncation
@@ -664,6 +675,9 @@ extern "C" vt_status vt_voronoi_adjacency(const float *points, uint32_t num_poin
     }
     g.lo = make_float3(bb[0], bb[2], bb[4]);
     g.inv_h = (float)(1.0 / h);
+#ifndef VT_VOR_THREAD_CELLS
+#define VT_VOR_THREAD_CELLS 0  // 1: the first pass builds one cell per thread
+#endif
 #ifndef VT_VOR_BOX
 #define VT_VOR_BOX 16.0f  // truncation box half-width in scene extents (measured: 4 -> 16 cuts the
                           // rows missing hull faces 5x for 40 % more build time)
@@ -690,7 +704,17 @@ extern "C" vt_status vt_voronoi_adjacency(const float *points, uint32_t num_poin
     for (int pass = 0; pass < 3 && ntodo > 0; ++pass) {
         uint32_t *out = bufs[pass & 1];
         cudaMemsetAsync(v.nretry, 0, 4, s);
-        if (pass < 2)
+        if (pass == 0 && !VT_VOR_THREAD_CELLS) {
+            // one warp per cell, persistent warps taking cells from a counter
+            uint32_t *next_cell = v.nretry + 4;
+            cudaMemsetAsync(next_cell, 0, 4, s);
+            int dev = 0, sms = 148;
+            cudaGetDevice(&dev);
+            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+            cell_warp_kernel<<<sms * 5, 32 * kWWarps, 0, s>>>(
+                points, n, g, v.start, v.sorted, nodes, ids, box, seed_adjacency, seed_offsets,
+                v.nbr, kMaxPlanes, v.count, out, v.nretry, next_cell);
+        } else if (pass < 2)
             cell_verify_kernel<<<vt::grid_for(ntodo, 64), 64, 0, s>>>(
                 points, n, g, v.start, v.sorted, nodes, ids, box, todo, ntodo,
                 pass == 0 ? kSeedK : kSeedKRetry, pass == 0 ? seed_adjacency : nullptr,
