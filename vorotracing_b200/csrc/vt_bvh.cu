@@ -305,8 +305,7 @@ extern "C" vt_status vt_bvh_build(const float *points, uint32_t num_points, void
     uint32_t *parent_leaf = (uint32_t *)w; w += align256((size_t)n * 4);
     uint32_t *parent_int = (uint32_t *)w;  w += align256((size_t)n * 4);
     uint32_t *flags = (uint32_t *)w;       w += align256((size_t)n * 4);
-    uint32_t *spare = (uint32_t *)w;       w += align256((size_t)n * 4);
-    (void)spare;
+    w += align256((size_t)n * 4);  // reserved (keeps the workspace layout of vt_bvh_workspace_bytes)
     size_t temp_bytes = vt::bvh::sort_temp_bytes(n);
     void *temp = w;
     Node *nd = (Node *)nodes;
