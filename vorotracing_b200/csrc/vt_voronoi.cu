@@ -708,10 +708,11 @@ extern "C" vt_status vt_voronoi_adjacency(const float *points, uint32_t num_poin
             // one warp per cell, persistent warps taking cells from a counter
             uint32_t *next_cell = v.nretry + 4;
             cudaMemsetAsync(next_cell, 0, 4, s);
-            int dev = 0, sms = 148;
+            int dev = 0, sms = 148, per_sm = 1;
             cudaGetDevice(&dev);
             cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-            cell_warp_kernel<<<sms * 5, 32 * kWWarps, 0, s>>>(
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, cell_warp_kernel, 32 * kWWarps, 0);
+            cell_warp_kernel<<<sms * (per_sm > 0 ? per_sm : 1), 32 * kWWarps, 0, s>>>(
                 points, n, g, v.start, v.sorted, nodes, ids, box, seed_adjacency, seed_offsets,
                 v.nbr, kMaxPlanes, v.count, out, v.nretry, next_cell);
         } else if (pass < 2)
