@@ -90,6 +90,10 @@ def test_render_host_roundtrip(c1_scene, c1_rays, transfer, bands):
     out = scene.render_host(host, transfer=transfer, bands=bands, weight_threshold=0.01)
     dev = scene.render(_dev(c1_rays), weight_threshold=0.01).cpu()
     assert torch.equal(out.view(torch.int16), dev.view(torch.int16))
+    # unpinned host buffers work too (staged through page-locked ones)
+    plain = scene.render_host(torch.from_numpy(c1_rays.copy()), torch.empty_like(out),
+                              transfer=transfer, bands=bands, weight_threshold=0.01)
+    assert torch.equal(plain.view(torch.int16), dev.view(torch.int16))
     # a second call reuses the device ray buffer; odd row counts leave a short last band
     out2 = scene.render_host(host[:-5].clone().pin_memory(), transfer=transfer, bands=bands, weight_threshold=0.01)
     assert torch.equal(out2.view(torch.int16), dev[:-5].view(torch.int16))

@@ -170,8 +170,16 @@ class InferScene:
             out_host = torch.empty(tuple(rays_host.shape[:-1]) + (4,), dtype=torch.float16,
                                    pin_memory=True)
         if transfer == "zero_copy":
-            if not rays_host.is_pinned():
+            if not (rays_host.is_pinned() and rays_host.is_contiguous()
+                    and rays_host.data_ptr() % 8 == 0):
                 rays_host = rays_host.contiguous().pin_memory()
+            if not (out_host.is_pinned() and out_host.is_contiguous()):
+                # the kernel writes page-locked memory only: render into a
+                # page-locked buffer and copy into the caller's
+                tmp = self.render_host(rays_host, None, transfer, bands, True, start_point,
+                                       per_ray_start, **kw)
+                out_host.copy_(tmp)
+                return out_host
             if per_ray_start and start_point is None:
                 rays_dev = rays_host.to(dev, non_blocking=True)
                 start_point = self.get_starting_point(rays_dev, per_ray=True)
