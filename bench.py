@@ -141,6 +141,16 @@ def compulsory_bytes(scene, rays, start, dbg_ops):
                                           textured_cells=int(tex.sum()))
 
 
+def algorithmic_bytes_per_ray(stats, tex_bytes: float) -> float:
+    """Bytes a ray touches by the reference's accounting: 40 B of ray I/O
+    (ray 24, start 4, permutation 4, rgba 8) plus, per visited cell, 28 B
+    (CSR offsets 8, winning neighbour id 4, next site 12, density 4), 8 B per
+    face tested (a half4 neighbour difference) and the cell's texels when it
+    is textured (64 B fp16, 24 B q8, 96 B fp32)."""
+    return (40.0 + 28.0 * float(stats["steps"]) + 8.0 * float(stats["faces"])
+            + tex_bytes * float(stats["textured"]))
+
+
 def cpu_oracle_rate(s, rays_np, start_idx, budget_s=15.0, threads=0, max_rays=None):
     """Rays/s of the CPU restatement on a strided sample sized to ~budget_s."""
     import oracle
@@ -205,6 +215,31 @@ def run_reference(args):
     print(json.dumps(out), flush=True)
 
 
+def training_leg(ws, rank, dev, steps):
+    """C4 training rays/s at this run's GPU count (every rank takes part):
+    one 1552x1040 camera per GPU on the 3M-site scene, fwd + bwd + NCCL
+    all-reduce of the 4.66 GB gradient bucket per step (weak scaling)."""
+    import torch
+
+    import bench_configs as bc
+
+    w = bc.c4_setup(ws, rank, dev, attrs_on_device=True)
+    r = bc.c4_measure(None, ws, dev, w, steps, 3)
+    res = {"metric": bc.C4_METRIC, "value": r["rays_per_s"], "unit": "rays/s",
+           "steps": steps, "warmup": 3, "ms_per_step": r["ms_per_step"],
+           "allreduce_ms_per_step": r["allreduce_ms"],
+           "allreduce_bus_gbs": r["allreduce_bus_gbs"], "grad_bucket_bytes": r["bucket_bytes"],
+           "scaling": "weak", "clocks": r["clocks"],
+           "config": {"workload": bc.C4_WORKLOAD, "sites": w["n"],
+                      "rays_per_step_per_gpu": w["nr"],
+                      "attributes": "drawn on the device (torch generator, same distributions "
+                                    "as the seeded numpy scene)",
+                      "l2": "flushed between timed steps (256 MB write)"}}
+    del w
+    torch.cuda.empty_cache()
+    return res
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -212,6 +247,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-train-leg", action="store_true",
+                    help="skip the C4 training leg of the C2 line")
     ap.add_argument("--transfer", default="zero_copy", choices=["zero_copy", "bands"],
                     help="e2e host I/O: the kernel reads/writes page-locked host memory "
                          "directly, or banded copies overlapped with the trace")
@@ -317,6 +354,8 @@ def main():
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
     step_ms, e2e_ms, trace_ms = (float(x) for x in t.cpu())
     if rank != 0:
+        if not args.no_train_leg:
+            training_leg(ws, rank, dev, min(args.steps, 10))
         torch.distributed.destroy_process_group()
         return
 
@@ -330,7 +369,12 @@ def main():
         peak_src = "measured"
     else:
         hbm, peak_src = 6650.0, "fallback"
-    achieved = comp / (trace_ms * 1e-3) / 1e9
+    # the contract's algorithmic bytes (the reference's per-cell reads):
+    # B_ray = 40 + sum over cells (28 + 8 * faces scanned + 64 if textured)
+    b_ray = algorithmic_bytes_per_ray(stats, 64.0)
+    alg = b_ray * nr
+    achieved = alg / (trace_ms * 1e-3) / 1e9
+    comp_achieved = comp / (trace_ms * 1e-3) / 1e9
     traffic = None
     warp_inst = None
     prof = os.path.join(ROOT, "profiles", "trace_infer_f16_c2.json")
@@ -367,15 +411,24 @@ def main():
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                      "frac": achieved / hbm, "traffic": traffic,
                      "peak_source": peak_src,
-                     "algorithmic_bytes_per_launch": comp,
+                     "bytes_per_ray": b_ray,
+                     "algorithmic_bytes_per_launch": alg,
+                     "formula": "B_ray = 40 + 28*steps + 8*faces + 64*textured (traversal "
+                                "means per ray); achieved = B_ray * rays / kernel_ms",
                      "kernel": "vt::infer_kernel<8, TexF16x4<8>>",
                      "kernel_ms": trace_ms},
+        "compulsory_roofline": {"achieved": comp_achieved, "peak": hbm, "unit": "GB/s",
+                                "frac": comp_achieved / hbm, "bytes_per_launch": comp,
+                                "what": "every visited cell's data once (16-B face rows, site, "
+                                        "density, texels) plus per-ray I/O"},
         "issue_roofline": issue,
         "traversal": stats,
         "clocks": clocks,
         # value loop: BVH query + trace; e2e loop: one BVH query + one trace per band
         "gpu_launches": 2 * args.steps + (1 + n_bands) * args.steps,
     }
+    if not args.no_train_leg:
+        out["training"] = training_leg(ws, rank, dev, min(args.steps, 10))
     if not args.no_cpu_baseline and ws == 1:
         import oracle
 

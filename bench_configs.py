@@ -118,15 +118,37 @@ def run_c3(args, ws, rank, dev):
               "strong", "f32", {"fps": 64 * args.steps / (ms * 1e-3)})
 
 
-def run_c4(args, ws, rank, dev):
-    from vorotracing_b200.cuda import _ops
+def c4_setup(ws, rank, dev, n_sites=None, attrs_on_device=False):
+    """The C4 training workload of this rank: scene tensors, this rank's
+    1552x1040 camera (orbit view = rank) in 4x8 tile order, broadcast start
+    cell, seeded target, gradient bucket and path record.
 
-    s = bench.load_scene(rank, ws, "C4", adjacency="gpu", n=args.sites)
-    t = _scene_tensors(s, dev)
-    W, H = sc.CONFIGS["C4"]["W"], sc.CONFIGS["C4"]["H"]
-    rays = torch.from_numpy(sc.pinhole_rays(sc.intrinsics(W, H), sc.orbit_pose(rank, 64), W, H)).to(dev)
+    attrs_on_device: draw density / texture logits with torch's generator on
+    the GPU (same distributions as scene.make_scene, other values) instead of
+    numpy on the host -- seconds instead of a minute per rank for the 4.6 GB
+    of texels, used by the training leg of ``bench.py --gpus N``."""
     from vorotracing_b200.cuda import NNBVH
+    from vorotracing_b200.cuda import _ops as ops_
 
+    c = sc.CONFIGS["C4"]
+    if attrs_on_device:
+        n = n_sites or c["n"]
+        pts = sc.make_sites(n, c["seed"], c["plane"])
+        t = {"points": torch.from_numpy(pts).to(dev)}
+        adj, offs, _ = ops_.build_voronoi_adjacency(t["points"], chunk_padding=sc.CSR_PAD)
+        t["adj"], t["offs"] = adj, offs
+        g = torch.Generator(device=dev).manual_seed(c["seed"] + 1000)
+        cols = 3 * c["res"] * c["res"]
+        t["density"] = torch.nn.functional.softplus(
+            torch.randn((n, 1), generator=g, device=dev))
+        t["diffuse"] = torch.rand((n, cols), generator=g, device=dev)
+        t["specular"] = torch.rand((n, cols), generator=g, device=dev) - 0.5
+    else:
+        s = bench.load_scene(rank, ws, "C4", adjacency="gpu", n=n_sites)
+        t = _scene_tensors(s, dev)
+    W, H = c["W"], c["H"]
+    rays = torch.from_numpy(sc.pinhole_rays(sc.intrinsics(W, H), sc.orbit_pose(rank, 64), W,
+                                            H)).to(dev)
     bvh = NNBVH()
     bvh.build(t["points"])
     st0 = bvh.query(t["points"], rays[0, 0, :3].reshape(1, 3))
@@ -136,8 +158,6 @@ def run_c4(args, ws, rank, dev):
     # Batch order is free in training (the reference samples patch-coherent
     # batches, vorotracing/datasets/datasets.py:238-241): rays and target go
     # in 4x8 tile order so that a warp traces neighbouring pixels.
-    from vorotracing_b200.cuda import _ops as ops_
-
     perm = ops_.tile_perm(H, W, device=dev).long()
     rays = rays.reshape(-1, 6)[perm].contiguous()
     target = target.reshape(-1, 3)[perm].contiguous()
@@ -148,6 +168,19 @@ def run_c4(args, ws, rank, dev):
     # the backward replays them without scanning faces or re-reading texels
     # (4 KB per ray)
     path = ops_.PathRecord(nr, 256, dev)
+    return dict(t=t, rays=rays, start=start, target=target, bucket=bucket, path=path, nr=nr,
+                n=n)
+
+
+def c4_step_fn(w, ar_events=None):
+    """One training step: face pack + forward (recording paths) + MSE
+    gradient + backward (replaying them) into the flat bucket + NCCL
+    all-reduce of the bucket.  ar_events: a list that receives an (start,
+    end) CUDA event pair around the all-reduce of every call."""
+    from vorotracing_b200.cuda import _ops
+
+    t, rays, start, target = w["t"], w["rays"], w["start"], w["target"]
+    bucket, path, nr = w["bucket"], w["path"], w["nr"]
 
     def step():
         faces = _ops.prefetch_faces(t["points"], t["adj"], t["offs"])
@@ -160,27 +193,67 @@ def run_c4(args, ws, rank, dev):
                                    t["adj"], t["offs"], rays, start, rgba, g, None, None, None,
                                    None, 0.0, dist_, None, Wt, St, tfar, WT, 1024, faces=faces,
                                    grads=bucket.views(), path=path, accumulate=False)
-        bucket.allreduce_()
+        if ar_events is not None:
+            e = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            e[0].record()
+            bucket.allreduce_()
+            e[1].record()
+            ar_events.append(e)
+        else:
+            bucket.allreduce_()
 
+    return step
+
+
+C4_METRIC = "training rays/s, fwd+bwd+grad all-reduce, 3M-site scene, 1552x1040 per GPU (C4)"
+C4_WORKLOAD = ("C4: 3M-site fp32 scene, R=8, one 1552x1040 camera per GPU vs a seeded U(0,1) "
+               "target, MSE; step = face pack + fwd (recording each ray's first 256 steps: "
+               "cell + colour) + bwd (replaying them) + NCCL all-reduce of the flat fp32 "
+               "gradient bucket; optimizer excluded")
+
+
+def c4_measure(args, ws, dev, w, steps, warmup):
+    """Times `steps` C4 steps (CUDA events, L2 flushed, max over ranks);
+    returns the step time, the all-reduce share and NCCL's bus bandwidth."""
+    ar = []
+    step = c4_step_fn(w, ar)
+
+    class A:
+        pass
+
+    a = A()
+    a.steps, a.warmup = steps, warmup
+    ms, clocks = Timer(a, dev).run(step, ws)
+    timed = ar[-steps:]
+    ar_ms = sum(x.elapsed_time(y) for x, y in timed) / steps
+    v = torch.tensor([ar_ms], dtype=torch.float64, device=dev)
+    if ws > 1:
+        torch.distributed.all_reduce(v, op=torch.distributed.ReduceOp.MAX)
+    ar_ms = float(v.item())
+    nbytes = w["bucket"].nbytes
+    busbw = (2.0 * (ws - 1) / ws * nbytes / (ar_ms * 1e-3) / 1e9) if ws > 1 and ar_ms > 0 else None
+    return dict(ms_total=ms, ms_per_step=ms / steps, clocks=clocks, allreduce_ms=ar_ms,
+                allreduce_bus_gbs=busbw, bucket_bytes=nbytes,
+                rays_per_s=w["nr"] * ws * steps / (ms * 1e-3))
+
+
+def run_c4(args, ws, rank, dev):
+    w = c4_setup(ws, rank, dev, n_sites=args.sites)
     if args.profile:
+        step = c4_step_fn(w)
         for _ in range(3):
             step()
         torch.cuda.synchronize()
         return
-    ms, clocks = Timer(args, dev).run(step, ws)
+    r = c4_measure(args, ws, dev, w, args.steps, args.warmup)
     if rank == 0:
-        rays_total = nr * ws * args.steps
-        _line(args, ws, "training rays/s, fwd+bwd+grad all-reduce, 3M-site scene, 1552x1040 per GPU (C4)",
-              rays_total / (ms * 1e-3), "rays/s", ms, clocks,
-              {"workload": "C4: 3M-site fp32 scene, R=8, one 1552x1040 camera per GPU vs a "
-                           "seeded U(0,1) target, MSE; step = face pack + fwd (recording each "
-                           "ray's first 256 steps: cell + colour) + bwd (replaying them) + NCCL "
-                           "all-reduce of the flat fp32 gradient bucket; optimizer excluded",
-               "sites": n, "rays_per_step_per_gpu": nr,
-               "grad_bucket_bytes": bucket.nbytes,
+        _line(args, ws, C4_METRIC, r["rays_per_s"], "rays/s", r["ms_total"], r["clocks"],
+              {"workload": C4_WORKLOAD, "sites": w["n"], "rays_per_step_per_gpu": w["nr"],
+               "grad_bucket_bytes": r["bucket_bytes"],
                "parallelism": f"data-parallel x{ws} (rays), scene replicated",
                "l2": "flushed between timed steps (256 MB write)"},
-              "weak", "f32")
+              "weak", "f32", {"allreduce_ms_per_step": r["allreduce_ms"],
+                              "allreduce_bus_gbs": r["allreduce_bus_gbs"]})
 
 
 def run_c5(args, ws, rank, dev):

@@ -14,6 +14,7 @@
  *
  * Reference interfaces replaced (paths inside the VoroTracing project):
  *   vt_prefetch_adj        trace_vorotracing_prefetch_adj, vorotracing/cuda/csrc/tracing/tracing_octmap.h:33-36
+ *   vt_prefetch_adj_diff   the same, also writing its (E+32, 4) half4 output, tracing_octmap.cu:612-640
  *   vt_trace_infer_f16     trace_vorotracing_infer,        tracing_octmap.h:38-51
  *   vt_trace_infer_q8      trace_vorotracing_infer_q8,     tracing_octmap.h:53-67
  *   vt_trace_fwd           trace_vorotracing_fwd,          tracing_octmap.h:11-31
@@ -92,6 +93,18 @@ VT_API uint64_t vt_face_rows(uint64_t csr_entries);
 VT_API vt_status vt_prefetch_adj(const float *points, uint32_t num_points, const uint32_t *adjacency,
                           uint64_t adjacency_len, const uint32_t *offsets, uint64_t csr_entries,
                           void *faces, uint64_t face_rows, uint32_t *err, vt_stream stream);
+/* Rows of the reference's adj_diff for an adjacency array of adjacency_len
+ * entries: adjacency_len + 32 (tracing_octmap.cu:624-625). */
+VT_API uint64_t vt_adj_diff_rows(uint64_t adjacency_len);
+/* vt_prefetch_adj plus, in the same pass, the reference's adj_diff array
+ * (trace_vorotracing_prefetch_adj, tracing_octmap.cu:612-640): adj_diff_rows
+ * rows of four binary16, half(points[adj[e]] - points[i]) and 0 for CSR entry
+ * e of cell i, zero rows after offsets[N].  adj_diff 8-byte aligned. */
+VT_API vt_status vt_prefetch_adj_diff(const float *points, uint32_t num_points,
+                                      const uint32_t *adjacency, uint64_t adjacency_len,
+                                      const uint32_t *offsets, uint64_t csr_entries, void *faces,
+                                      uint64_t face_rows, void *adj_diff, uint64_t adj_diff_rows,
+                                      uint32_t *err, vt_stream stream);
 
 /* ---- inference ---- */
 
@@ -242,7 +255,7 @@ VT_API vt_status vt_bvh_build(const float *points, uint32_t num_points, void *no
 /* Same build as vt_bvh_build, for callers that cannot allocate device
  * memory (an application that lends this library only its input and output
  * buffers, or a binding without a CUDA allocator): its scratch is a fixed
- * 32 MiB array inside the library, held on every GPU that loads it, so it
+ * 40 MiB array inside the library, held on every GPU that loads it, so it
  * takes no workspace argument and accepts at most VT_BVH_NOALLOC_MAX_POINTS
  * sites (more: VT_ERR_INVALID).  The first call on a device looks up the
  * array's device address; make it before any stream capture.  Calls share

@@ -99,6 +99,28 @@ def test_render_host_roundtrip(c1_scene, c1_rays, transfer, bands):
     assert torch.equal(out2.view(torch.int16), dev[:-5].view(torch.int16))
 
 
+def test_render_host_async_unpinned_rays(c1_scene, c1_rays):
+    """sync=False with unpinned rays: the staged page-locked copy stays alive
+    while the trace reads it, even when other page-locked buffers are
+    allocated and scribbled on before the trace finishes."""
+    from vorotracing_b200.render import InferScene
+
+    s = c1_scene
+    scene = InferScene(_dev(s["points"]), _dev(s["density"]), _dev(s["adj"]), _dev(s["offs"]),
+                       _dev(s["diffuse"]), _dev(s["specular"]))
+    want = scene.render(_dev(c1_rays), weight_threshold=0.01).cpu()
+    outs = []
+    for _ in range(4):
+        outs.append(scene.render_host(torch.from_numpy(c1_rays.copy()), sync=False,
+                                      weight_threshold=0.01))
+        junk = torch.empty(c1_rays.shape, dtype=torch.float32, pin_memory=True)
+        junk.fill_(float("nan"))
+        del junk
+    torch.cuda.synchronize()
+    for o in outs:
+        assert torch.equal(o.view(torch.int16), want.view(torch.int16))
+
+
 @pytest.mark.parametrize("mode", ["mean", "quantile"])
 def test_render_depth_matches_oracle(c1_scene, c1_rays, mode):
     """Fused depth render vs the oracle's training forward with the same

@@ -61,6 +61,18 @@ def test_noalloc_build_matches_workspace_build_twice():
         np.testing.assert_array_equal(_query(L, got, pts, q), _query(L, ref, pts, q))
 
 
+def test_noalloc_build_at_the_limit():
+    """Exactly VT_BVH_NOALLOC_MAX_POINTS sites fit the fixed array."""
+    from vorotracing_b200._lib import lib
+
+    L = lib()
+    n = 1_048_576
+    rng = np.random.default_rng(1)
+    pts = torch.from_numpy(rng.uniform(-2, 2, (n, 3)).astype(np.float32)).cuda()
+    ref, got = _build_both(L, pts)
+    assert torch.equal(ref, got)
+
+
 def test_noalloc_rejects_too_many_sites():
     from vorotracing_b200._lib import lib
 

@@ -30,27 +30,55 @@ class VtDebug(C.Structure):
                 ("visited", C.c_void_p), ("textured", C.c_void_p)]
 
 
+def load(path: str = LIB_PATH, require_all: bool = True):
+    """Open a build of the library and declare the non-int return types.
+    require_all: every entry point the header declares must be exported."""
+    if not os.path.exists(path):
+        raise RuntimeError(
+            f"vorotracing_b200: CUDA library not built ({path}); run "
+            "`python -m vorotracing_b200.build` (there is no CPU fallback)")
+    L = C.CDLL(path)
+    L.vt_last_error.restype = C.c_char_p
+    L.vt_version.restype = C.c_char_p
+    L.vt_face_rows.restype = C.c_uint64
+    L.vt_face_rows.argtypes = [C.c_uint64]
+    L.vt_adj_diff_rows.restype = C.c_uint64
+    L.vt_adj_diff_rows.argtypes = [C.c_uint64]
+    if require_all:
+        for name in exported_symbols():
+            getattr(L, name)  # every declared entry point must be exported
+    for name in ("vt_bvh_nodes_bytes", "vt_bvh_workspace_bytes", "vt_morton_workspace_bytes",
+                 "vt_trace_bwd_workspace_bytes"):
+        if hasattr(L, name):
+            getattr(L, name).restype = C.c_uint64
+    return L
+
+
 def lib():
     """Load the library (raises RuntimeError when it is absent)."""
     global _lib
     if _lib is None:
-        if not os.path.exists(LIB_PATH):
-            raise RuntimeError(
-                f"vorotracing_b200: CUDA library not built ({LIB_PATH}); run "
-                "`python -m vorotracing_b200.build` (there is no CPU fallback)")
-        L = C.CDLL(LIB_PATH)
-        L.vt_last_error.restype = C.c_char_p
-        L.vt_version.restype = C.c_char_p
-        L.vt_face_rows.restype = C.c_uint64
-        L.vt_face_rows.argtypes = [C.c_uint64]
-        for name in exported_symbols():
-            getattr(L, name)  # every declared entry point must be exported
-        for name in ("vt_bvh_nodes_bytes", "vt_bvh_workspace_bytes", "vt_morton_workspace_bytes",
-                     "vt_trace_bwd_workspace_bytes"):
-            if hasattr(L, name):
-                getattr(L, name).restype = C.c_uint64
-        _lib = L
+        _lib = load()
     return _lib
+
+
+class using:
+    """Route the operators through another build of the library for the
+    duration of a ``with`` block (the tests' fast-math measurement build)."""
+
+    def __init__(self, other):
+        self.other = other
+
+    def __enter__(self):
+        global _lib
+        lib()
+        self.saved, _lib = _lib, self.other
+        return self.other
+
+    def __exit__(self, *exc):
+        global _lib
+        _lib = self.saved
+        return False
 
 
 def exported_symbols():

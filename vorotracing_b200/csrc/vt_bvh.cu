@@ -257,11 +257,17 @@ __global__ void query_kernel(const Node *__restrict__ nodes, const uint32_t *__r
 
 inline size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
+// Scratch of the radix sort.  If cub's size query fails, an upper bound is
+// returned instead of its (then undefined) answer: the sort's alternate key
+// and value buffers plus 1 MiB for its histograms, so a workspace sized from
+// this value is never too small.
 size_t sort_temp_bytes(uint32_t n)
 {
     size_t bytes = 0;
-    cub::DeviceRadixSort::SortPairs(nullptr, bytes, (const uint32_t *)nullptr, (uint32_t *)nullptr,
-                                    (const uint32_t *)nullptr, (uint32_t *)nullptr, (int)n, 0, 30);
+    cudaError_t e = cub::DeviceRadixSort::SortPairs(nullptr, bytes, (const uint32_t *)nullptr,
+                                                    (uint32_t *)nullptr, (const uint32_t *)nullptr,
+                                                    (uint32_t *)nullptr, (int)n, 0, 30);
+    if (e != cudaSuccess) return (size_t)n * 8 + (size_t(1) << 20);
     return bytes;
 }
 
@@ -379,7 +385,10 @@ extern "C" vt_status vt_bvh_query_hint(const void *nodes, const float *points, u
 // device current) and caches it; make that first call before any stream
 // capture.  All calls share the one array, so calls whose work overlaps on
 // the GPU (different streams, or different host threads on one device) race
-// on it; serialise them.  The array keeps the previous call's contents: every
+// on it; serialise them.  The cached address belongs to the device's primary
+// context: after cudaDeviceReset (or anything else that destroys that
+// context) this library must be unloaded and loaded again before the next
+// call.  The array keeps the previous call's contents: every
 // field the build reads (bounding box, sort buffers, parent links, the
 // per-node arrival counters) is rewritten by the build before it is read.
 // ---------------------------------------------------------------------------
@@ -387,7 +396,11 @@ extern "C" vt_status vt_bvh_query_hint(const void *nodes, const float *points, u
 
 namespace {
 
-constexpr size_t kNoAllocScratchBytes = size_t(32) << 20;
+// vt_bvh_workspace_bytes(VT_BVH_NOALLOC_MAX_POINTS) is 28 MiB + 256 B of
+// build buffers plus the radix sort's scratch, which holds alternate key and
+// value buffers (8 MiB) and its histograms: 40 MiB covers it with room to
+// spare (the build checks the exact need on every call).
+constexpr size_t kNoAllocScratchBytes = size_t(40) << 20;
 static __device__ __align__(256) unsigned char g_bvh_noalloc_scratch[kNoAllocScratchBytes];
 
 std::mutex g_noalloc_mu;

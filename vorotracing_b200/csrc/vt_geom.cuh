@@ -112,8 +112,12 @@ __device__ __forceinline__ V3 probe_dir(const Ray &ray, float t0, V3 P)
     V3 dd = hit - P;
     float len = norm(dd);
     if (len > 1e-8f) {
+#ifdef VT_REF_FASTMATH
+        return mk(dd.x / len, dd.y / len, dd.z / len);  // the reference's d /= len
+#else
         float inv = 1.0f / len;
         return mk(dd.x * inv, dd.y * inv, dd.z * inv);
+#endif
     }
     return ray.d;
 }

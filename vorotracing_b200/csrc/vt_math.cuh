@@ -29,6 +29,16 @@ __device__ __forceinline__ float pow2i(int k)  // 2^k for k in [-126, 127]
     return __int_as_float((k + 127) << 23);
 }
 
+#ifdef VT_REF_FASTMATH
+// Measurement build only (libvorotracing_b200_refmath.so, never the product):
+// the reference's arithmetic, compiled like vorotracing/cuda/_backend.py:188-204
+// (-use_fast_math, contraction on), so that CUDA's fast expf / logf and
+// approximate division stand where the reference has them.  Tests compare
+// this build with the exact one to bound how far the reference binary's
+// results can sit from the oracle's.
+__device__ __forceinline__ float expf_exact(float x) { return expf(x); }
+__device__ __forceinline__ float logf_exact(float x) { return logf(x); }
+#else
 __device__ __forceinline__ float expf_exact(float x)
 {
     if (x != x) return x;
@@ -83,6 +93,7 @@ __device__ __forceinline__ float logf_exact(float x)
     float ef = (float)e;
     return fmaf(ef, kLn2Hi, fmaf(ef, kLn2Lo, lm));
 }
+#endif
 
 __device__ __forceinline__ float sigmoid(float x) { return 1.0f / (1.0f + expf_exact(-x)); }
 

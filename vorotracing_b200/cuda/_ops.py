@@ -80,6 +80,57 @@ def prefetch_faces(points, adjacency, offsets) -> torch.Tensor:
     return faces
 
 
+def prefetch_adj_diff(points, adjacency, offsets) -> torch.Tensor:
+    """The reference's adj_diff, (adjacency_len + 32, 4) binary16 rows
+    (trace_vorotracing_prefetch_adj, tracing_octmap.cu:612-640; rows after
+    offsets[N] are zero here, uninitialised there).  The packed face rows the
+    trace kernels read are written in the same pass and travel with the
+    returned tensor (``adj_diff._vt_faces``), so passing it back to the
+    inference operators costs nothing extra."""
+    points = points.contiguous()
+    adjacency = adjacency.contiguous()
+    offsets = offsets.contiguous()
+    n = points.size(0)
+    e = adjacency.numel()
+    csr = int(offsets[-1].item()) if offsets.numel() else 0
+    L = lib()
+    # as many face rows as prefetch_faces makes; rows from offsets[N] on are zero
+    faces = torch.empty((int(L.vt_face_rows(C.c_uint64(e))), FACE_ROW_HALVES),
+                        dtype=torch.float16, device=points.device)
+    drows = int(L.vt_adj_diff_rows(C.c_uint64(e)))
+    adj_diff = torch.empty((drows, 4), dtype=torch.float16, device=points.device)
+    err = torch.zeros(1, dtype=torch.int32, device=points.device)
+    check(L.vt_prefetch_adj_diff(ptr(points), C.c_uint32(n), ptr(adjacency), C.c_uint64(e),
+                                 ptr(offsets), C.c_uint64(csr), ptr(faces),
+                                 C.c_uint64(faces.size(0)), ptr(adj_diff), C.c_uint64(drows),
+                                 ptr(err), stream_ptr(points.device)), "vt_prefetch_adj_diff")
+    if int(err.item()) != 0:
+        _fail("invalid Voronoi adjacency: neighbour index out of range, offsets not monotone "
+              "or a cell degree above 65535")
+    adj_diff._vt_faces = faces
+    return adj_diff
+
+
+def _resolve_faces(adjacent_diff, adjacency, points, offsets) -> torch.Tensor:
+    """The packed face rows behind an ``adjacent_diff`` argument: the tensor
+    itself when it is this package's packed layout, the rows built alongside
+    it by prefetch_adj_diff, or (a reference-layout array from elsewhere)
+    rows built now from the sites and CSR and kept on that array."""
+    if (adjacent_diff.dtype == torch.float16 and adjacent_diff.dim() == 2
+            and adjacent_diff.size(1) == 4):
+        if adjacent_diff.device != points.device:
+            _fail("adjacent_diff must be on the points' device")
+        if adjacent_diff.size(0) < adjacency.numel():
+            _fail("adjacent_diff must have at least as many rows as point_adjacency")
+        faces = getattr(adjacent_diff, "_vt_faces", None)
+        if faces is None or faces.device != points.device:
+            faces = prefetch_faces(points, adjacency, offsets)
+            adjacent_diff._vt_faces = faces
+        return faces
+    _check_faces(adjacent_diff, adjacency, points)
+    return adjacent_diff
+
+
 def make_scene(points, density, offsets, faces) -> _lib.VtScene:
     return _lib.VtScene(points.data_ptr(), density.data_ptr(), offsets.data_ptr(),
                         faces.data_ptr(), points.size(0), faces.size(0))
@@ -88,8 +139,8 @@ def make_scene(points, density, offsets, faces) -> _lib.VtScene:
 def _check_faces(faces, adjacency, points):
     if (faces.dtype != torch.float16 or faces.dim() != 2 or faces.size(1) != FACE_ROW_HALVES
             or faces.size(0) < adjacency.numel()):
-        _fail("adjacent_diff must be the packed face tensor returned by prefetch_octmap_adj "
-              "of this package for the same adjacency")
+        _fail("adjacent_diff must be the (E+32, 4) float16 array returned by "
+              "prefetch_octmap_adj, or this package's packed face rows, for the same adjacency")
     if faces.device != points.device:
         _fail("adjacent_diff must be on the points' device")
 
@@ -184,7 +235,7 @@ def _infer_common(points, diffuse, specular, density, adjacency, offsets, rays, 
     n = points.size(0)
     if diffuse.size(0) != n or specular.size(0) != n or density.numel() != n:
         _fail("diffuse, specular, density must each have num_points rows")
-    _check_faces(adjacent_diff, adjacency, points)
+    faces = _resolve_faces(adjacent_diff, adjacency, points, offsets)
     res = _res_from(diffuse, 3 if q8 else 4)
     if _res_from(specular, 3 if q8 else 4) != res:
         _fail("diffuse and specular octahedral resolutions must match")
@@ -210,7 +261,7 @@ def _infer_common(points, diffuse, specular, density, adjacency, offsets, rays, 
             _fail("out must be on the rays' device")
         rays_p, rgba_p = ptr(rays), ptr(rgba)
     err = torch.zeros(1, dtype=torch.int32, device=dev)
-    scene = make_scene(points, density, offsets, adjacent_diff)
+    scene = make_scene(points, density, offsets, faces)
     dbg, keep = _debug_struct(debug, nr, n)
     L = lib()
     stream = stream_ptr(dev)
@@ -634,9 +685,6 @@ def trace_vorotracing_bwd(points, diffuse, specular, density, adjacency, offsets
     else:
         # caller-provided (e.g. views of a flat all-reduce bucket)
         points_grad, diffuse_grad, specular_grad, density_grad = grads
-        if not accumulate and not overwrite:
-            for t in grads:
-                t.zero_()
         if (points_grad.shape != (n, 3) or points_grad.dtype != torch.float32
                 or diffuse_grad.shape != diffuse.shape or diffuse_grad.dtype != diffuse.dtype
                 or specular_grad.shape != specular.shape
@@ -645,6 +693,9 @@ def trace_vorotracing_bwd(points, diffuse, specular, density, adjacency, offsets
                 or not all(t.is_contiguous() for t in grads)):
             _fail("grads must be contiguous (points (N,3) f32, diffuse / specular like the "
                   "attributes, density (N,) f32)")
+        if not accumulate and not overwrite:
+            for t in grads:
+                t.zero_()
     ray_grad = torch.empty_like(rays)
     if faces is None:
         faces = prefetch_faces(points, adjacency, offsets)

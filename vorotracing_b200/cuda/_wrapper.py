@@ -105,12 +105,14 @@ class TraceVoroTracing(torch.autograd.Function):
 
 
 def prefetch_octmap_adj(points, adjacency, offsets):
-    """Scene face layout for the inference operators (_wrapper.py:234-237).
+    """Neighbour differences for the inference operators (_wrapper.py:234-237).
 
-    Returns this package's packed face rows (16 bytes per CSR entry) instead of
-    the reference's (E+32, 4) half offsets; callers only pass it back to
-    trace_octmap_infer / trace_octmap_infer_q8."""
-    return _ops.prefetch_faces(points, adjacency, offsets)
+    Returns the reference's array: (len(adjacency) + 32, 4) float16 rows
+    half(points[adj[e]] - points[i]), 0 (tracing_octmap.cu:612-640), which
+    callers may keep and export (scripts/export_for_viewer.py writes it into
+    V3 .foam files).  The packed face rows the kernels read are built in the
+    same pass and ride along on the returned tensor."""
+    return _ops.prefetch_adj_diff(points, adjacency, offsets)
 
 
 def trace_octmap_infer(points, diffuse_fp16, specular_fp16, density, adjacency, offsets, rays,

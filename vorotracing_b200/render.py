@@ -163,16 +163,21 @@ class InferScene:
         ``per_ray_start`` is given; the first ray's origin is the only part
         copied ahead.  With ``sync=False`` the call returns once the work is
         queued and the current stream is ordered after it, so an event
-        recorded there afterwards marks completion."""
+        recorded there afterwards marks completion; rays that had to be
+        staged into page-locked memory are kept alive by the scene until the
+        trace that reads them has finished."""
         dev = self.primal_points.device
         cur = torch.cuda.current_stream(dev)
+        self._staged = [(t, e) for t, e in getattr(self, "_staged", []) if not e.query()]
         if out_host is None:
             out_host = torch.empty(tuple(rays_host.shape[:-1]) + (4,), dtype=torch.float16,
                                    pin_memory=True)
         if transfer == "zero_copy":
+            staged = False
             if not (rays_host.is_pinned() and rays_host.is_contiguous()
                     and rays_host.data_ptr() % 8 == 0):
                 rays_host = rays_host.contiguous().pin_memory()
+                staged = True
             if not (out_host.is_pinned() and out_host.is_contiguous()):
                 # the kernel writes page-locked memory only: render into a
                 # page-locked buffer and copy into the caller's
@@ -190,6 +195,14 @@ class InferScene:
             self.render(rays_host, start_point=start_point, out=out_host, host_io=True, **kw)
             if sync:
                 cur.synchronize()
+            elif staged:
+                # the kernel reads the staging buffer through its raw address,
+                # which torch's host allocator does not track: hold the buffer
+                # until an event behind the trace has completed, or the
+                # allocator could hand it to the next pin_memory() mid-trace
+                done = torch.cuda.Event()
+                done.record(cur)
+                self._staged.append((rays_host, done))
             return out_host
         if transfer != "bands":
             raise ValueError(f"unknown transfer mode {transfer!r}")
