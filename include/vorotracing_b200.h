@@ -206,7 +206,8 @@ VT_API vt_status vt_trace_bwd(const vt_scene *scene, int attr_half, const void *
 /* Optional scratch of vt_trace_bwd (256-byte aligned): with it the texel and
  * site gradients accumulate in padded fp32 rows with one vector atomic per
  * texel (instead of three scalar atomics) and are added to the outputs at the
- * end; fp16 gradients are then summed in fp32 and rounded once.  Pass null
+ * end; fp16 gradients (point_error included) are then summed in fp32 and
+ * rounded once.  Pass null
  * to accumulate straight into the outputs. */
 VT_API uint64_t vt_trace_bwd_workspace_bytes(uint32_t num_points, int res);
 

@@ -99,6 +99,7 @@ template <class AT> struct BwdIn {
     float *density_grad;
     AT *point_error;
     float4 *sdiff, *sspec, *spts;  // padded scratch or null
+    float *sperr;                  // fp32 point_error scratch or null
     PathRec rec;                   // forward's path record or null cells
 };
 
@@ -170,6 +171,7 @@ __global__ void __launch_bounds__(kTrainBlock, VT_BWD_MIN_BLOCKS)
     I.sdiff = b.sdiff;
     I.sspec = b.sspec;
     I.spts = b.spts;
+    I.sperr = b.sperr;
     I.prev_geom = I.prev_grad = I.cur_grad = I.next_grad = mk(0.f, 0.f, 0.f);
     I.prev_idx = 0xffffffffu;
     float tu, tv;
@@ -218,6 +220,15 @@ __global__ void compact4_kernel(const float4 *__restrict__ scratch, uint64_t n, 
     }
 }
 
+// out[t] (+)= scratch[t]: the fp32 point_error sums rounded once.
+template <class AT, bool kSet>
+__global__ void compact1_kernel(const float *__restrict__ scratch, uint64_t n, AT *__restrict__ out)
+{
+    uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= n) return;
+    out[t] = kSet ? fromf<AT>(scratch[t]) : fromf<AT>(tof<AT>(out[t]) + scratch[t]);
+}
+
 inline size_t a256(size_t x) { return (x + 255) & ~(size_t)255; }
 
 vt_status fill_common(TrainCommon &a, const vt_scene *scene, const float *rays, uint32_t nr,
@@ -262,14 +273,16 @@ vt_status launch_bwd(const TrainCommon &a, const void *dif, const void *spe, Bwd
         b.sdiff = (float4 *)w;
         b.sspec = (float4 *)(w + a256(ntex * 16));
         b.spts = (float4 *)(w + 2 * a256(ntex * 16));
-        cudaError_t e = cudaMemsetAsync(ws, 0, 2 * a256(ntex * 16) + a256((size_t)a.n_points * 16), s);
+        const size_t perr_off = 2 * a256(ntex * 16) + a256((size_t)a.n_points * 16);
+        b.sperr = b.point_error ? (float *)(w + perr_off) : nullptr;
+        cudaError_t e = cudaMemsetAsync(
+            ws, 0, perr_off + (b.point_error ? a256((size_t)a.n_points * 4) : 0), s);
         if (e == cudaSuccess && overwrite)  // the outputs the kernels add to directly
             e = cudaMemsetAsync(b.density_grad, 0, (size_t)a.n_points * 4, s);
-        if (e == cudaSuccess && overwrite && b.point_error)
-            e = cudaMemsetAsync(b.point_error, 0, (size_t)a.n_points * sizeof(AT), s);
         if (e != cudaSuccess) return set_error(VT_ERR_CUDA, "vt_trace_bwd memset: %s", cudaGetErrorString(e));
     } else {
         b.sdiff = b.sspec = b.spts = nullptr;
+        b.sperr = nullptr;
     }
     const int F = (a.K > 0 && a.dq ? kBwdDepth : 0) | (b.dist_grad ? kBwdDist : 0) |
                   (b.ray_error && b.point_error ? kBwdErr : 0);
@@ -293,11 +306,17 @@ vt_status launch_bwd(const TrainCommon &a, const void *dif, const void *spe, Bwd
         compact4_kernel<AT, true><<<grid_for(ntex, 256), 256, 0, s>>>(b.sspec, ntex, b.specular_grad);
         compact4_kernel<float, true><<<grid_for(a.n_points, 256), 256, 0, s>>>(b.spts, a.n_points,
                                                                                 b.points_grad);
+        if (b.sperr)
+            compact1_kernel<AT, true><<<grid_for(a.n_points, 256), 256, 0, s>>>(
+                b.sperr, a.n_points, b.point_error);
     } else if (ws) {
         compact4_kernel<AT, false><<<grid_for(ntex, 256), 256, 0, s>>>(b.sdiff, ntex, b.diffuse_grad);
         compact4_kernel<AT, false><<<grid_for(ntex, 256), 256, 0, s>>>(b.sspec, ntex, b.specular_grad);
         compact4_kernel<float, false><<<grid_for(a.n_points, 256), 256, 0, s>>>(b.spts, a.n_points,
                                                                                  b.points_grad);
+        if (b.sperr)
+            compact1_kernel<AT, false><<<grid_for(a.n_points, 256), 256, 0, s>>>(
+                b.sperr, a.n_points, b.point_error);
     }
     return check_launch("bwd_kernel");
 }
@@ -353,7 +372,8 @@ extern "C" vt_status vt_trace_fwd(const vt_scene *scene, int attr_half, const vo
 extern "C" uint64_t vt_trace_bwd_workspace_bytes(uint32_t num_points, int res)
 {
     const uint64_t ntex = (uint64_t)num_points * res * res;
-    return 2 * vt::a256(ntex * 16) + vt::a256((size_t)num_points * 16);
+    return 2 * vt::a256(ntex * 16) + vt::a256((size_t)num_points * 16) +
+           vt::a256((size_t)num_points * 4);
 }
 
 extern "C" vt_status vt_trace_bwd(const vt_scene *scene, int attr_half, const void *diffuse,

@@ -176,6 +176,7 @@ template <class AT, int R, int F = kBwdDepth | kBwdDist | kBwdErr> struct BwdInt
     // with vector atomics (1 instead of 3 per texel); null = scalar atomics
     // straight into the outputs.
     float4 *sdiff, *sspec, *spts;
+    float *sperr;  // fp32 point_error scratch (with the padded scratch), else null
     float *dden;
     AT *perr;
     V3 prev_geom, prev_grad, cur_grad, next_grad;
@@ -299,7 +300,10 @@ template <class AT, int R, int F = kBwdDepth | kBwdDist | kBwdErr> struct BwdInt
         if (delta > 0.0f) dadd = s * (1.0f - alpha);
         acc = acc + w * rgb;
         if constexpr ((F & kBwdErr) != 0)
-            if (perr) atomic_add<AT>(perr + cell, w * ray_error);
+            if (sperr)
+                atomicAdd(sperr + cell, w * ray_error);
+            else if (perr)
+                atomic_add<AT>(perr + cell, w * ray_error);
         V3 dLdrgb = mk(g_rgb.x * w, g_rgb.y * w, g_rgb.z * w);
         V3 rest = divs(fwd_rgb - acc, T * ((1.0f - alpha) + 1e-6f));
         float dLda = T * dot(rgb - rest, g_rgb);
