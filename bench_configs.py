@@ -82,6 +82,29 @@ def _line(args, ws, metric, value, unit, ms_total, clocks, config, scaling, dtyp
     print(json.dumps(out), flush=True)
 
 
+def cpu_sample_rate(run, rays, budget_s=10.0):
+    """Rays/s of a CPU oracle call ``run(sample_rays)`` on a strided sample of
+    ``rays`` (N, 6) sized to about budget_s seconds; returns (rate, n, s)."""
+    probe = rays[:: max(1, len(rays) // 1024)]
+    t = time.perf_counter()
+    run(probe)
+    rate = len(probe) / max(time.perf_counter() - t, 1e-6)
+    n = int(min(len(rays), max(1024, rate * budget_s)))
+    sample = rays[:: max(1, len(rays) // n)][:n]
+    t = time.perf_counter()
+    run(sample)
+    dt = time.perf_counter() - t
+    return len(sample) / dt, len(sample), dt
+
+
+def _cpu_line(rate, n, dt, total, unit_scale, unit, what):
+    import oracle
+
+    return {"value": rate / unit_scale, "unit": unit, "cores": oracle.max_threads(),
+            "kind": "port",
+            "sample": f"{n} of {total} rays (strided), {dt:.1f} s; {what}"}
+
+
 def _scene_tensors(s, dev):
     d = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
     return {k: d(s[k]) for k in ("points", "density", "adj", "offs", "diffuse", "specular")}
@@ -107,6 +130,24 @@ def run_c3(args, ws, rank, dev):
             scene.render(r, start_point=st, weight_threshold=WT, cell_skip_threshold=SKIP)
 
     ms, clocks = Timer(args, dev).run(step, ws)
+    extra = {"fps": 64 * args.steps / (ms * 1e-3)}
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        import oracle
+
+        q8 = tuple(np.float32(v) for v in (scene.diff_scale, scene.diff_offset,
+                                           scene.spec_scale, scene.spec_offset))
+        h = lambda x: x.detach().cpu().numpy()
+        S = oracle.Scene(h(scene.primal_points), h(scene.point_adjacency),
+                         h(scene.point_adjacency_offsets), h(scene.density), h(scene.diffuse_q8),
+                         h(scene.specular_q8), oracle.ATTR_U8, q8=q8)
+        r0 = views[0].reshape(-1, 6).cpu().numpy()
+        st0 = int(starts[0].reshape(-1)[0])
+        thr = oracle.max_threads()
+        rate, n, dt = cpu_sample_rate(
+            lambda r: oracle.trace_infer(S, r, np.full(len(r), st0, np.uint32), wt=WT,
+                                         skip=SKIP, threads=thr), r0)
+        extra["cpu_baseline"] = _cpu_line(rate, n, dt, len(r0), 1e6, "Mrays/s",
+                                          "q8 inference of view 0 by the CPU restatement")
     if rank == 0:
         rays = 64 * W * H * args.steps
         _line(args, ws, "Mrays/s q8 forward render, 64 views 1296x840, 1M-site scene (C3)",
@@ -115,7 +156,7 @@ def run_c3(args, ws, rank, dev):
                            "orbit views (radius 3, elevation 15 deg), view-sharded",
                "views_per_step": 64, "parallelism": f"views round-robin over {ws} GPU(s)",
                "l2": "flushed between timed steps (256 MB write)"},
-              "strong", "f32", {"fps": 64 * args.steps / (ms * 1e-3)})
+              "strong", "f32", extra)
 
 
 def c4_setup(ws, rank, dev, n_sites=None, attrs_on_device=False):
@@ -246,14 +287,38 @@ def run_c4(args, ws, rank, dev):
         torch.cuda.synchronize()
         return
     r = c4_measure(args, ws, dev, w, args.steps, args.warmup)
+    extra = {"allreduce_ms_per_step": r["allreduce_ms"],
+             "allreduce_bus_gbs": r["allreduce_bus_gbs"]}
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        import oracle
+
+        h = lambda x: x.detach().cpu().numpy()
+        t = w["t"]
+        S = oracle.Scene(h(t["points"]), h(t["adj"]), h(t["offs"]), h(t["density"]),
+                         h(t["diffuse"]), h(t["specular"]), oracle.ATTR_F32)
+        rays_h = h(w["rays"])
+        st0 = int(w["start"][0])
+        thr = oracle.max_threads()
+
+        def train(rr):
+            st = np.full(len(rr), st0, np.uint32)
+            f = oracle.trace_fwd(S, rr, st, wt=WT, threads=thr)
+            g = np.zeros_like(f["rgba"])
+            g[:, :3] = (2.0 / (len(rr) * 3)) * (f["rgba"][:, :3] - 0.5)
+            oracle.trace_bwd(S, rr, st, f["rgba"], g, W=f["W"], S=f["S"], t_far=f["t_far"],
+                             distortion=f["distortion"], wt=WT, threads=thr)
+
+        rate, n, dt = cpu_sample_rate(train, rays_h)
+        extra["cpu_baseline"] = _cpu_line(rate, n, dt, len(rays_h), 1.0, "rays/s",
+                                          "training forward + backward by the CPU restatement "
+                                          "(no all-reduce)")
     if rank == 0:
         _line(args, ws, C4_METRIC, r["rays_per_s"], "rays/s", r["ms_total"], r["clocks"],
               {"workload": C4_WORKLOAD, "sites": w["n"], "rays_per_step_per_gpu": w["nr"],
                "grad_bucket_bytes": r["bucket_bytes"],
                "parallelism": f"data-parallel x{ws} (rays), scene replicated",
                "l2": "flushed between timed steps (256 MB write)"},
-              "weak", "f32", {"allreduce_ms_per_step": r["allreduce_ms"],
-                              "allreduce_bus_gbs": r["allreduce_bus_gbs"]})
+              "weak", "f32", extra)
 
 
 def run_c5(args, ws, rank, dev):
@@ -287,6 +352,26 @@ def run_c5(args, ws, rank, dev):
             scene.render(r, weight_threshold=WT, cell_skip_threshold=SKIP, per_ray_start=True)
 
     ms, clocks = Timer(args, dev).run(step, ws)
+    extra = {}
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        import oracle
+
+        h = lambda x: x.detach().cpu().numpy()
+        S = oracle.Scene(h(scene.primal_points), h(scene.point_adjacency),
+                         h(scene.point_adjacency_offsets), h(scene.density),
+                         h(scene.diffuse_fp16), h(scene.specular_fp16), oracle.ATTR_F16X4)
+        allr = np.concatenate([h(f).reshape(-1, 6) for f in frames])
+        pts = h(scene.primal_points)
+        thr = oracle.max_threads()
+
+        def infer(rr):
+            st = oracle.nn_query(pts, rr[:, :3], threads=thr).astype(np.uint32)
+            oracle.trace_infer(S, rr, st, wt=WT, skip=SKIP, threads=thr)
+
+        rate, n, dt = cpu_sample_rate(infer, allr)
+        extra["cpu_baseline"] = _cpu_line(rate, n, dt, len(allr), 1e6, "Mrays/s",
+                                          "per-ray brute-force start cell + fp16 inference by "
+                                          "the CPU restatement, all three cameras")
     tot = torch.tensor([nr], dtype=torch.float64, device=dev)
     if ws > 1:
         torch.distributed.all_reduce(tot)
@@ -300,7 +385,7 @@ def run_c5(args, ws, rank, dev):
                "rays_per_step": int(tot.item()),
                "parallelism": f"4-row bands round-robin over {ws} GPU(s)",
                "l2": "flushed between timed steps (256 MB write)"},
-              "strong", "f32")
+              "strong", "f32", extra)
 
 
 def run(args):
