@@ -34,6 +34,32 @@ def test_bvh_matches_brute_force(c1_scene):
         np.testing.assert_array_equal(got, ref)
 
 
+@pytest.mark.parametrize("spread", [0.0, 1e-3, 2e-2, 0.3])
+def test_bvh_warp_cooperative_queries(c1_scene, spread):
+    """Warps of 32 close queries (ray origins of a tile, a lens aperture) take
+    the warp-cooperative traversal, scattered ones the per-lane search; either
+    way every answer is the brute-force (d2, lowest id) minimum, with and
+    without hints.  Spread 0 puts 32 identical queries in a warp, and some
+    clusters sit exactly between sites (ties)."""
+    from vorotracing_b200.cuda import NNBVH
+
+    pts = c1_scene["points"]
+    rng = np.random.default_rng(11)
+    centres = np.concatenate([rng.uniform(-2.5, 2.5, (60, 3)),
+                              0.5 * (pts[:4] + pts[4:8])]).astype(np.float32)
+    q = (np.repeat(centres, 32, axis=0)
+         + spread * rng.standard_normal((len(centres) * 32, 3))).astype(np.float32)
+    q = np.concatenate([q, rng.uniform(-3, 3, (17, 3)).astype(np.float32)])  # ragged last warp
+    b = NNBVH()
+    b.build(_dev(pts))
+    ref = oracle.nn_query(pts, q)
+    np.testing.assert_array_equal(b.query(_dev(pts), _dev(q)).cpu().numpy(), ref)
+    for hint in (torch.tensor([int(ref[0])]), torch.tensor([len(pts) - 1]),
+                 torch.from_numpy(np.roll(ref, 1).astype(np.int32))):
+        got = b.query(_dev(pts), _dev(q), hint=hint.cuda()).cpu().numpy()
+        np.testing.assert_array_equal(got, ref)
+
+
 @pytest.mark.parametrize("n", [1, 2, 3, 33])
 def test_bvh_tiny_and_duplicates(n):
     from vorotracing_b200.cuda import nearest_neighbor_bvh

@@ -179,27 +179,13 @@ __device__ __forceinline__ void visit_leaf(const float *__restrict__ p, uint32_t
 // A hint (a site believed nearest, e.g. the answer for a neighbouring query)
 // only seeds the bound: the result is the same lexicographic (d2, id) minimum,
 // found with tighter pruning when the hint is good.
-__global__ void query_kernel(const Node *__restrict__ nodes, const uint32_t *__restrict__ ids,
-                             const float *__restrict__ p, uint32_t n,
-                             const float *__restrict__ queries, uint32_t nq,
-                             const uint32_t *__restrict__ hint, uint32_t hint_count, int32_t *out,
-                             uint32_t *err)
+// Depth-first search from the root for one query: nearest child first,
+// subtrees pruned when their bound exceeds the best d2 so far.
+__device__ __forceinline__ void query_thread(const Node *__restrict__ nodes,
+                                             const uint32_t *__restrict__ ids,
+                                             const float *__restrict__ p, V3 q, float &best,
+                                             uint32_t &bi, uint32_t *err)
 {
-    uint32_t t = blockIdx.x * blockDim.x + threadIdx.x;
-    if (t >= nq) return;
-    V3 q = mk(__ldg(queries + (size_t)t * 3), __ldg(queries + (size_t)t * 3 + 1),
-              __ldg(queries + (size_t)t * 3 + 2));
-    float best = __int_as_float(0x7f800000);
-    uint32_t bi = 0xffffffffu;
-    if (hint) {
-        const uint32_t h = __ldg(hint + (hint_count == 1 ? 0 : t));
-        if (h < n) visit_leaf(p, h, q, best, bi);
-    }
-    if (n == 1) {
-        visit_leaf(p, 0, q, best, bi);
-        out[t] = (int32_t)bi;
-        return;
-    }
     uint32_t stack[kStack];
     int sp = 0;
     uint32_t cur = 0;
@@ -252,7 +238,172 @@ __global__ void query_kernel(const Node *__restrict__ nodes, const uint32_t *__r
         }
         if (!found) break;
     }
+}
+
+// A hint (a site believed nearest, e.g. the answer for a neighbouring query)
+// only seeds the bound: the result is the same lexicographic (d2, id) minimum,
+// found with tighter pruning when the hint is good.
+__global__ void query_kernel(const Node *__restrict__ nodes, const uint32_t *__restrict__ ids,
+                             const float *__restrict__ p, uint32_t n,
+                             const float *__restrict__ queries, uint32_t nq,
+                             const uint32_t *__restrict__ hint, uint32_t hint_count, int32_t *out,
+                             uint32_t *err)
+{
+    uint32_t t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= nq) return;
+    V3 q = mk(__ldg(queries + (size_t)t * 3), __ldg(queries + (size_t)t * 3 + 1),
+              __ldg(queries + (size_t)t * 3 + 2));
+    float best = __int_as_float(0x7f800000);
+    uint32_t bi = 0xffffffffu;
+    if (hint) {
+        const uint32_t h = __ldg(hint + (hint_count == 1 ? 0 : t));
+        if (h < n) visit_leaf(p, h, q, best, bi);
+    }
+    if (n == 1)
+        visit_leaf(p, 0, q, best, bi);
+    else
+        query_thread(nodes, ids, p, q, best, bi, err);
     out[t] = (int32_t)bi;
+}
+
+// Warp-cooperative query (packet traversal).  The 32 lanes of a warp hold 32
+// queries, in the callers' order neighbouring ray origins, and, when they are
+// close together (see below), walk the tree together: one warp-uniform current node and one warp-wide stack (entry k in
+// register k / 32 of lane k % 32, popped by a shuffle).  A child is entered
+// when any lane's bound admits it (ballot), nearer child first by lane vote,
+// and a leaf child is visited at once.  Node and site loads are warp-uniform
+// (one broadcast transaction) and no lane diverges from the traversal.  Each
+// lane still prunes with its own bound, so its answer is the same
+// lexicographic (d2, id) minimum as query_kernel's: the warp visits a
+// superset of the subtrees each lane needs.  Lanes past nq take part with an
+// empty bound (best < 0 admits nothing).
+__global__ void __launch_bounds__(128) query_warp_kernel(
+    const Node *__restrict__ nodes, const uint32_t *__restrict__ ids, const float *__restrict__ p,
+    uint32_t n, const float *__restrict__ queries, uint32_t nq, const uint32_t *__restrict__ hint,
+    uint32_t hint_count, int32_t *out, uint32_t *err)
+{
+    const uint32_t t = blockIdx.x * blockDim.x + threadIdx.x;
+    const uint32_t lane = threadIdx.x & 31u;
+    const bool valid = t < nq;
+    V3 q = mk(0.f, 0.f, 0.f);
+    float best = -1.0f;
+    uint32_t bi = 0xffffffffu;
+    if (valid) {
+        q = mk(__ldg(queries + (size_t)t * 3), __ldg(queries + (size_t)t * 3 + 1),
+               __ldg(queries + (size_t)t * 3 + 2));
+        best = __int_as_float(0x7f800000);
+        if (hint) {
+            const uint32_t h = __ldg(hint + (hint_count == 1 ? 0 : t));
+            if (h < n) visit_leaf(p, h, q, best, bi);
+        }
+    }
+    if (__ballot_sync(0xffffffffu, valid) == 0) return;
+    if (n == 1) {
+        if (valid) {
+            visit_leaf(p, 0, q, best, bi);
+            out[t] = (int32_t)bi;
+        }
+        return;
+    }
+    // The warp traverses together only when its queries are close compared
+    // with the typical distance between sites, s = (scene box volume / n)^(1/3),
+    // the scale of a nearest-site search ball: the squared diagonal of the
+    // queries' box at most 16 s^2.  The lanes' search balls then overlap and
+    // their union is little more than one.  Otherwise every lane searches on
+    // its own (a warp of scattered queries would visit the union of all their
+    // searches).
+    float lo[3] = {q.x, q.y, q.z}, hi[3] = {q.x, q.y, q.z};
+    if (!valid) {
+        lo[0] = lo[1] = lo[2] = __int_as_float(0x7f800000);
+        hi[0] = hi[1] = hi[2] = __int_as_float(0xff800000);
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+#pragma unroll
+        for (int a = 0; a < 3; ++a) {
+            lo[a] = fminf(lo[a], __shfl_xor_sync(0xffffffffu, lo[a], o));
+            hi[a] = fmaxf(hi[a], __shfl_xor_sync(0xffffffffu, hi[a], o));
+        }
+    }
+    const V3 ext = mk(hi[0] - lo[0], hi[1] - lo[1], hi[2] - lo[2]);
+    const float diag2 = dot(ext, ext);
+    const Node root = nodes[0];
+    const float vol = fmaxf((root.hi[0] - root.lo[0]) * (root.hi[1] - root.lo[1]) *
+                                (root.hi[2] - root.lo[2]),
+                            0.0f);
+    const float spacing = cbrtf(vol / (float)n);
+    const bool packet = diag2 <= 16.0f * spacing * spacing;
+    if (!packet) {
+        if (valid) {
+            query_thread(nodes, ids, p, q, best, bi, err);
+            out[t] = (int32_t)bi;
+        }
+        return;
+    }
+    uint32_t st0 = 0, st1 = 0, st2 = 0;  // the warp's stack, distributed over the lanes
+    int sp = 0;
+    uint32_t cur = 0;
+    bool overflow = false;
+    for (;;) {
+        // cur is an internal node here
+        const Node nd = nodes[cur];
+        const uint32_t c[2] = {nd.left, nd.right};
+        float dd[2];
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            if (c[k] & kLeaf) {
+                const uint32_t id = __ldg(ids + (c[k] & ~kLeaf));
+                if (valid) visit_leaf(p, id, q, best, bi);
+                dd[k] = __int_as_float(0x7f800000);  // visited: nothing left below
+            } else {
+                dd[k] = valid ? box_d2(nodes[c[k]], q) : __int_as_float(0x7f800000);
+            }
+        }
+        const bool need0 = __any_sync(0xffffffffu, dd[0] <= best);
+        const bool need1 = __any_sync(0xffffffffu, dd[1] <= best);
+        if (need0 && need1) {
+            const int votes1 = __popc(__ballot_sync(0xffffffffu, valid && dd[1] < dd[0]));
+            const int votes0 = __popc(__ballot_sync(0xffffffffu, valid && dd[0] < dd[1]));
+            const int nearc = votes1 > votes0 ? 1 : 0;
+            if (sp >= 3 * 32) {
+                overflow = true;
+                break;
+            }
+            const uint32_t far = c[1 - nearc];
+            if ((uint32_t)(sp & 31) == lane) {
+                if (sp < 32) st0 = far;
+                else if (sp < 64) st1 = far;
+                else st2 = far;
+            }
+            sp++;
+            cur = c[nearc];
+            continue;
+        }
+        if (need0) {
+            cur = c[0];
+            continue;
+        }
+        if (need1) {
+            cur = c[1];
+            continue;
+        }
+        // pop the next subtree that any lane can still improve in
+        bool found = false;
+        while (sp > 0) {
+            --sp;
+            const uint32_t reg = sp < 32 ? st0 : (sp < 64 ? st1 : st2);
+            const uint32_t sub = __shfl_sync(0xffffffffu, reg, sp & 31);
+            const float d = valid ? box_d2(nodes[sub], q) : __int_as_float(0x7f800000);
+            if (__any_sync(0xffffffffu, d <= best)) {
+                cur = sub;
+                found = true;
+                break;
+            }
+        }
+        if (!found) break;
+    }
+    if (overflow && lane == 0) report(err, VT_ERR_DATA);
+    if (valid) out[t] = (int32_t)bi;
 }
 
 inline size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
@@ -276,6 +427,13 @@ size_t sort_temp_bytes(uint32_t n)
 
 using vt::bvh::align256;
 using vt::bvh::Node;
+
+// Batches of at least this many queries use the warp-cooperative traversal
+// (building with -DVT_WARP_QUERY_MIN=0xffffffff keeps every batch per-thread).
+#ifndef VT_WARP_QUERY_MIN
+#define VT_WARP_QUERY_MIN 32
+#endif
+static constexpr uint32_t kWarpQueryMin = VT_WARP_QUERY_MIN;
 
 extern "C" uint64_t vt_bvh_nodes_bytes(uint32_t num_points)
 {
@@ -343,8 +501,13 @@ extern "C" vt_status vt_bvh_query(const void *nodes, const float *points, uint32
     const Node *nd = (const Node *)nodes;
     const uint32_t *ids =
         (const uint32_t *)((const char *)nodes + align256((size_t)(num_points - 1) * sizeof(Node)));
-    vt::bvh::query_kernel<<<vt::grid_for(num_queries, 128), 128, 0, (cudaStream_t)stream>>>(
-        nd, ids, points, num_points, queries, num_queries, nullptr, 0, out, err);
+    if (num_queries >= kWarpQueryMin)
+        vt::bvh::query_warp_kernel<<<vt::grid_for(num_queries, 128), 128, 0,
+                                     (cudaStream_t)stream>>>(nd, ids, points, num_points, queries,
+                                                             num_queries, nullptr, 0, out, err);
+    else
+        vt::bvh::query_kernel<<<vt::grid_for(num_queries, 128), 128, 0, (cudaStream_t)stream>>>(
+            nd, ids, points, num_points, queries, num_queries, nullptr, 0, out, err);
     return vt::check_launch("vt_bvh_query");
 }
 
@@ -362,8 +525,14 @@ extern "C" vt_status vt_bvh_query_hint(const void *nodes, const float *points, u
     const Node *nd = (const Node *)nodes;
     const uint32_t *ids =
         (const uint32_t *)((const char *)nodes + align256((size_t)(num_points - 1) * sizeof(Node)));
-    vt::bvh::query_kernel<<<vt::grid_for(num_queries, 128), 128, 0, (cudaStream_t)stream>>>(
-        nd, ids, points, num_points, queries, num_queries, hint, hint_count, out, err);
+    if (num_queries >= kWarpQueryMin)
+        vt::bvh::query_warp_kernel<<<vt::grid_for(num_queries, 128), 128, 0,
+                                     (cudaStream_t)stream>>>(nd, ids, points, num_points, queries,
+                                                             num_queries, hint, hint_count, out,
+                                                             err);
+    else
+        vt::bvh::query_kernel<<<vt::grid_for(num_queries, 128), 128, 0, (cudaStream_t)stream>>>(
+            nd, ids, points, num_points, queries, num_queries, hint, hint_count, out, err);
     return vt::check_launch("vt_bvh_query_hint");
 }
 
