@@ -215,7 +215,7 @@ def run_reference(args):
     print(json.dumps(out), flush=True)
 
 
-def training_leg(ws, rank, dev, steps):
+def training_leg(ws, rank, dev, steps, allreduce="peer"):
     """C4 training rays/s at this run's GPU count (every rank takes part):
     one 1552x1040 camera per GPU on the 3M-site scene, fwd + bwd + NCCL
     all-reduce of the 4.66 GB gradient bucket per step (weak scaling)."""
@@ -223,12 +223,13 @@ def training_leg(ws, rank, dev, steps):
 
     import bench_configs as bc
 
-    w = bc.c4_setup(ws, rank, dev, attrs_on_device=True)
+    w = bc.c4_setup(ws, rank, dev, attrs_on_device=True, allreduce=allreduce)
     r = bc.c4_measure(None, ws, dev, w, steps, 3)
     res = {"metric": bc.C4_METRIC, "value": r["rays_per_s"], "unit": "rays/s",
            "steps": steps, "warmup": 3, "ms_per_step": r["ms_per_step"],
            "allreduce_ms_per_step": r["allreduce_ms"],
            "allreduce_bus_gbs": r["allreduce_bus_gbs"], "grad_bucket_bytes": r["bucket_bytes"],
+           "allreduce": r["allreduce"], "peer_check": r["peer_check"],
            "scaling": "weak", "clocks": r["clocks"],
            "config": {"workload": bc.C4_WORKLOAD, "sites": w["n"],
                       "rays_per_step_per_gpu": w["nr"],
@@ -247,6 +248,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--allreduce", default="peer", choices=["peer", "nccl"],
+                    help="C4 gradient reduction at N>1: the fused compaction + all-reduce over "
+                         "peer memory, or the compaction then NCCL's all-reduce")
     ap.add_argument("--no-train-leg", action="store_true",
                     help="skip the C4 training leg of the C2 line")
     ap.add_argument("--transfer", default="zero_copy", choices=["zero_copy", "bands"],
@@ -355,7 +359,7 @@ def main():
     step_ms, e2e_ms, trace_ms = (float(x) for x in t.cpu())
     if rank != 0:
         if not args.no_train_leg:
-            training_leg(ws, rank, dev, min(args.steps, 10))
+            training_leg(ws, rank, dev, min(args.steps, 10), args.allreduce)
         torch.distributed.destroy_process_group()
         return
 
@@ -428,7 +432,7 @@ def main():
         "gpu_launches": 2 * args.steps + (1 + n_bands) * args.steps,
     }
     if not args.no_train_leg:
-        out["training"] = training_leg(ws, rank, dev, min(args.steps, 10))
+        out["training"] = training_leg(ws, rank, dev, min(args.steps, 10), args.allreduce)
     if not args.no_cpu_baseline and ws == 1:
         import oracle
 

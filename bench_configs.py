@@ -159,7 +159,7 @@ def run_c3(args, ws, rank, dev):
               "strong", "f32", extra)
 
 
-def c4_setup(ws, rank, dev, n_sites=None, attrs_on_device=False):
+def c4_setup(ws, rank, dev, n_sites=None, attrs_on_device=False, allreduce="peer"):
     """The C4 training workload of this rank: scene tensors, this rank's
     1552x1040 camera (orbit view = rank) in 4x8 tile order, broadcast start
     cell, seeded target, gradient bucket and path record.
@@ -209,19 +209,53 @@ def c4_setup(ws, rank, dev, n_sites=None, attrs_on_device=False):
     # the backward replays them without scanning faces or re-reading texels
     # (4 KB per ray)
     path = ops_.PathRecord(nr, 256, dev)
-    return dict(t=t, rays=rays, start=start, target=target, bucket=bucket, path=path, nr=nr,
-                n=n)
+    w = dict(t=t, rays=rays, start=start, target=target, bucket=bucket, path=path, nr=nr, n=n,
+             reducer=None, allreduce="nccl" if ws == 1 else allreduce)
+    if ws > 1 and allreduce == "peer":
+        from vorotracing_b200.shard import PeerGradReducer
+
+        w["reducer"] = PeerGradReducer(bucket, c["res"])
+        w["peer_check"] = _check_peer_reduce(w)
+    return w
 
 
-def c4_step_fn(w, ar_events=None):
+def _check_peer_reduce(w):
+    """One step's gradients reduced both ways, the fused peer kernel and
+    NCCL's all-reduce of the compacted bucket: the largest difference
+    relative to the gradient's scale (summation orders differ)."""
+    c4_step_fn(w, reduce=False)()
+    red = w["reducer"]
+    red.reduce_()
+    peer = w["bucket"].flat.clone()
+    w_n = dict(w, reducer=None, allreduce="nccl")
+    c4_step_fn(w_n)()
+    torch.cuda.synchronize()
+    ref = w["bucket"].flat
+    scale = float(ref.abs().max())
+    diff = float((peer - ref).abs().max())
+    del peer
+    return {"max_abs_diff": diff, "scale": scale, "rel": diff / scale if scale else 0.0}
+
+
+def c4_step_fn(w, ar_events=None, reduce=True):
     """One training step: face pack + forward (recording paths) + MSE
-    gradient + backward (replaying them) into the flat bucket + NCCL
-    all-reduce of the bucket.  ar_events: a list that receives an (start,
-    end) CUDA event pair around the all-reduce of every call."""
+    gradient + backward (replaying them) into the flat bucket + the
+    all-reduce of the bucket: NCCL's, or (w["reducer"]) the fused
+    compaction + reduction over peer memory.  ar_events: a list that
+    receives an (start, end) CUDA event pair around the reduction of every
+    call; reduce=False stops after the backward."""
     from vorotracing_b200.cuda import _ops
 
     t, rays, start, target = w["t"], w["rays"], w["start"], w["target"]
     bucket, path, nr = w["bucket"], w["path"], w["nr"]
+    red = w.get("reducer")
+    bw = dict(workspace=red.workspace, keep_workspace=True) if red is not None else {}
+
+    def do_reduce():
+        if red is not None:
+            red.reduce_()
+        else:
+            bucket.allreduce_()
 
     def step():
         faces = _ops.prefetch_faces(t["points"], t["adj"], t["offs"])
@@ -233,15 +267,17 @@ def c4_step_fn(w, ar_events=None):
         _ops.trace_vorotracing_bwd(t["points"], t["diffuse"], t["specular"], t["density"],
                                    t["adj"], t["offs"], rays, start, rgba, g, None, None, None,
                                    None, 0.0, dist_, None, Wt, St, tfar, WT, 1024, faces=faces,
-                                   grads=bucket.views(), path=path, accumulate=False)
+                                   grads=bucket.views(), path=path, accumulate=False, **bw)
+        if not reduce:
+            return
         if ar_events is not None:
             e = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
             e[0].record()
-            bucket.allreduce_()
+            do_reduce()
             e[1].record()
             ar_events.append(e)
         else:
-            bucket.allreduce_()
+            do_reduce()
 
     return step
 
@@ -274,12 +310,13 @@ def c4_measure(args, ws, dev, w, steps, warmup):
     nbytes = w["bucket"].nbytes
     busbw = (2.0 * (ws - 1) / ws * nbytes / (ar_ms * 1e-3) / 1e9) if ws > 1 and ar_ms > 0 else None
     return dict(ms_total=ms, ms_per_step=ms / steps, clocks=clocks, allreduce_ms=ar_ms,
-                allreduce_bus_gbs=busbw, bucket_bytes=nbytes,
+                allreduce_bus_gbs=busbw, bucket_bytes=nbytes, allreduce=w["allreduce"],
+                peer_check=w.get("peer_check"),
                 rays_per_s=w["nr"] * ws * steps / (ms * 1e-3))
 
 
 def run_c4(args, ws, rank, dev):
-    w = c4_setup(ws, rank, dev, n_sites=args.sites)
+    w = c4_setup(ws, rank, dev, n_sites=args.sites, allreduce=args.allreduce)
     if args.profile:
         step = c4_step_fn(w)
         for _ in range(3):
@@ -288,7 +325,8 @@ def run_c4(args, ws, rank, dev):
         return
     r = c4_measure(args, ws, dev, w, args.steps, args.warmup)
     extra = {"allreduce_ms_per_step": r["allreduce_ms"],
-             "allreduce_bus_gbs": r["allreduce_bus_gbs"]}
+             "allreduce_bus_gbs": r["allreduce_bus_gbs"], "allreduce": r["allreduce"],
+             "peer_check": r["peer_check"]}
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         import oracle
 

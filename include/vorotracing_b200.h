@@ -203,6 +203,11 @@ VT_API vt_status vt_trace_bwd(const vt_scene *scene, int attr_half, const void *
  * overwritten instead of accumulated into, so they need no zero
  * initialisation (requires the workspace). */
 #define VT_BWD_OVERWRITE 1u
+/* VT_BWD_KEEP_WORKSPACE (with VT_BWD_OVERWRITE): leave the texel and site
+ * sums in the workspace instead of writing them to the outputs (density_grad
+ * is still written); vt_grad_allreduce_peer then reduces them across ranks
+ * straight into every rank's gradient bucket. */
+#define VT_BWD_KEEP_WORKSPACE 2u
 /* Optional scratch of vt_trace_bwd (256-byte aligned): with it the texel and
  * site gradients accumulate in padded fp32 rows with one vector atomic per
  * texel (instead of three scalar atomics) and are added to the outputs at the
@@ -210,6 +215,42 @@ VT_API vt_status vt_trace_bwd(const vt_scene *scene, int attr_half, const void *
  * rounded once.  Pass null
  * to accumulate straight into the outputs. */
 VT_API uint64_t vt_trace_bwd_workspace_bytes(uint32_t num_points, int res);
+
+/* ---- multi-GPU gradient reduction over peer memory ---- */
+
+/* CUDA IPC of device buffers between the processes of one node: the handle
+ * (64 bytes) and byte offset of `ptr` inside its allocation; a handle
+ * opened by another process (vt_ipc_open, which maps the whole allocation;
+ * add the offset) and its release.  No reference counterpart: the
+ * reference trains on one GPU. */
+VT_API vt_status vt_ipc_handle(const void *ptr, void *handle64, uint64_t *offset);
+VT_API vt_status vt_ipc_open(const void *handle64, void **base);
+VT_API vt_status vt_ipc_close(void *base);
+
+#define VT_PEER_MAX 8
+/* Every rank's backward workspace (written by vt_trace_bwd with
+ * VT_BWD_KEEP_WORKSPACE) and flat f32 gradient bucket [points 3N | density N |
+ * diffuse 3R^2 N | specular 3R^2 N], as device addresses valid on the
+ * calling GPU (its own, or peers' opened with vt_ipc_open).  fp32 attributes
+ * only. */
+typedef struct {
+    uint32_t world;
+    uint32_t num_points;
+    int32_t res;
+    const void *workspace[VT_PEER_MAX];
+    float *bucket[VT_PEER_MAX];
+} vt_peer_grads;
+/* The all-reduce of the training step, fused with the workspace compaction:
+ * rank `rank` sums its 1/world share of every gradient (texels and sites
+ * from the workspaces, densities from the buckets) over the ranks in rank
+ * order 0..world-1 and writes the sums into that share of every rank's bucket
+ * by peer stores, so every rank ends with bit-identical buckets.  Every
+ * rank's backward must be complete before the call (e.g. a stream-ordered
+ * collective as a fence), and no rank may read its bucket or reuse its
+ * workspace until every rank's call has completed.  Replaces the
+ * vt_trace_bwd compaction plus an NCCL all-reduce of the bucket. */
+VT_API vt_status vt_grad_allreduce_peer(const vt_peer_grads *grads, uint32_t rank,
+                                        vt_stream stream);
 
 /* ---- cameras (ray generation for the benchmark views) ---- */
 

@@ -19,6 +19,7 @@ STRUCTS = {
     "vt_debug": ("vorotracing_b200._lib", "VtDebug"),
     "vt_path": ("vorotracing_b200._lib", "VtPath"),
     "vt_camera": ("vorotracing_b200.cameras", "VtCamera"),
+    "vt_peer_grads": ("vorotracing_b200._lib", "VtPeerGrads"),
 }
 
 

@@ -30,6 +30,14 @@ class VtDebug(C.Structure):
                 ("visited", C.c_void_p), ("textured", C.c_void_p)]
 
 
+PEER_MAX = 8
+
+
+class VtPeerGrads(C.Structure):
+    _fields_ = [("world", C.c_uint32), ("num_points", C.c_uint32), ("res", C.c_int32),
+                ("workspace", C.c_void_p * PEER_MAX), ("bucket", C.c_void_p * PEER_MAX)]
+
+
 def load(path: str = LIB_PATH, require_all: bool = True):
     """Open a build of the library and declare the non-int return types.
     require_all: every entry point the header declares must be exported."""

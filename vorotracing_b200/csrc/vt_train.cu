@@ -264,7 +264,7 @@ vt_status launch_fwd(const TrainCommon &a, const void *dif, const void *spe, con
 
 template <class AT, int R>
 vt_status launch_bwd(const TrainCommon &a, const void *dif, const void *spe, BwdIn<AT> b,
-                     void *ws, bool overwrite, cudaStream_t s)
+                     void *ws, bool overwrite, bool keep_ws, cudaStream_t s)
 {
     TexPlain<AT, R> t{(const AT *)dif, (const AT *)spe};
     const uint64_t ntex = (uint64_t)a.n_points * R * R;
@@ -301,7 +301,10 @@ vt_status launch_bwd(const TrainCommon &a, const void *dif, const void *spe, Bwd
         VT_BWD_CASE(4) VT_BWD_CASE(5) VT_BWD_CASE(6) VT_BWD_CASE(7)
 #undef VT_BWD_CASE
     }
-    if (ws && overwrite) {
+    if (keep_ws) {
+        // the texel, site and point_error sums stay in the workspace for
+        // vt_grad_allreduce_peer, which reduces and compacts them across ranks
+    } else if (ws && overwrite) {
         compact4_kernel<AT, true><<<grid_for(ntex, 256), 256, 0, s>>>(b.sdiff, ntex, b.diffuse_grad);
         compact4_kernel<AT, true><<<grid_for(ntex, 256), 256, 0, s>>>(b.sspec, ntex, b.specular_grad);
         compact4_kernel<float, true><<<grid_for(a.n_points, 256), 256, 0, s>>>(b.spts, a.n_points,
@@ -402,6 +405,9 @@ extern "C" vt_status vt_trace_bwd(const vt_scene *scene, int attr_half, const vo
     VT_REQUIRE(!(flags & VT_BWD_OVERWRITE) || workspace,
                "vt_trace_bwd: VT_BWD_OVERWRITE needs the workspace");
     const bool overwrite = (flags & VT_BWD_OVERWRITE) != 0;
+    const bool keep_ws = (flags & VT_BWD_KEEP_WORKSPACE) != 0;
+    VT_REQUIRE(!keep_ws || (overwrite && workspace),
+               "vt_trace_bwd: VT_BWD_KEEP_WORKSPACE needs VT_BWD_OVERWRITE and the workspace");
     if (st != VT_OK) return st;
     VT_REQUIRE(diffuse && specular, "vt_trace_bwd: null textures");
     VT_REQUIRE(num_rays == 0 || (rgba && rgba_grad), "vt_trace_bwd: null rgba inputs");
@@ -436,8 +442,10 @@ extern "C" vt_status vt_trace_bwd(const vt_scene *scene, int attr_half, const vo
                             (__half *)diffuse_grad, (__half *)specular_grad, density_grad,
                             (__half *)point_error};
         b.rec = rec;
-        if (res == 8) return vt::launch_bwd<__half, 8>(a, diffuse, specular, b, workspace, overwrite, s);
-        if (res == 4) return vt::launch_bwd<__half, 4>(a, diffuse, specular, b, workspace, overwrite, s);
+        if (res == 8)
+            return vt::launch_bwd<__half, 8>(a, diffuse, specular, b, workspace, overwrite, keep_ws, s);
+        if (res == 4)
+            return vt::launch_bwd<__half, 4>(a, diffuse, specular, b, workspace, overwrite, keep_ws, s);
     } else {
         vt::BwdIn<float> b{quantile_indices, (const float *)rgba, (const float *)rgba_grad,
                            depth_grad, (const float *)ray_error, contribution_alpha_grad,
@@ -445,8 +453,10 @@ extern "C" vt_status vt_trace_bwd(const vt_scene *scene, int attr_half, const vo
                            (float *)diffuse_grad, (float *)specular_grad, density_grad,
                            (float *)point_error};
         b.rec = rec;
-        if (res == 8) return vt::launch_bwd<float, 8>(a, diffuse, specular, b, workspace, overwrite, s);
-        if (res == 4) return vt::launch_bwd<float, 4>(a, diffuse, specular, b, workspace, overwrite, s);
+        if (res == 8)
+            return vt::launch_bwd<float, 8>(a, diffuse, specular, b, workspace, overwrite, keep_ws, s);
+        if (res == 4)
+            return vt::launch_bwd<float, 4>(a, diffuse, specular, b, workspace, overwrite, keep_ws, s);
     }
     return vt::set_error(VT_ERR_INVALID, "vt_trace_bwd: res must be 4 or 8, got %d", res);
 }

@@ -600,7 +600,8 @@ def trace_vorotracing_bwd(points, diffuse, specular, density, adjacency, offsets
                           distortion_grad, W_total, S_total, t_far, weight_threshold: float,
                           max_intersections: int, faces=None, grads=None,
                           vector_atomics: bool = True, path: PathRecord | None = None,
-                          accumulate: bool = True):
+                          accumulate: bool = True, workspace: torch.Tensor | None = None,
+                          keep_workspace: bool = False):
     """Training backward (tracing_octmap.cu:860-1103).  Gradients go to new
     tensors, or into ``grads`` = (points, diffuse, specular, density) when
     given: added to them, or (``accumulate=False``) overwriting them, which
@@ -608,7 +609,12 @@ def trace_vorotracing_bwd(points, diffuse, specular, density, adjacency, offsets
     point_error); ray_grad is allocated and never written, as in the
     reference; point_error is None unless ray_error is given.  ``path``: the
     PathRecord filled by the forward of the same inputs (the walk then skips
-    the face scan of the recorded steps; results are unchanged)."""
+    the face scan of the recorded steps; results are unchanged).
+    ``workspace``: a caller-owned uint8 device tensor of at least
+    vt_trace_bwd_workspace_bytes (e.g. one mapped by the other ranks);
+    ``keep_workspace`` (with grads, accumulate=False): leave the texel and
+    site sums in it for shard.PeerGradReducer instead of writing them to
+    ``grads`` (density is written)."""
     points, diffuse, specular = points.contiguous(), diffuse.contiguous(), specular.contiguous()
     density, adjacency, offsets = density.contiguous(), adjacency.contiguous(), offsets.contiguous()
     rays, start_point = _aligned(rays, 8), start_point.contiguous()
@@ -702,9 +708,20 @@ def trace_vorotracing_bwd(points, diffuse, specular, density, adjacency, offsets
     scene = make_scene(points, density, offsets, faces)
     err = torch.zeros(1, dtype=torch.int32, device=dev)
     ws, wsb = None, 0
+    if keep_workspace and (not vector_atomics or not overwrite or workspace is None
+                           or ray_error is not None or half):
+        _fail("keep_workspace needs fp32 attributes, vector_atomics, accumulate=False, a caller "
+              "workspace and no ray_error")
     if vector_atomics:
         wsb = int(lib().vt_trace_bwd_workspace_bytes(C.c_uint32(n), C.c_int(res)))
-        ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
+        if workspace is not None:
+            if (workspace.dtype != torch.uint8 or workspace.numel() < wsb
+                    or workspace.device != dev or workspace.data_ptr() % 256):
+                _fail(f"workspace must be a 256-byte aligned uint8 tensor of >= {wsb} bytes on "
+                      "the rays' device")
+            ws, wsb = workspace, workspace.numel()
+        else:
+            ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
     check(lib().vt_trace_bwd(C.byref(scene), C.c_int(half), ptr(diffuse), ptr(specular),
                              C.c_int(res), ptr(rays), C.c_uint32(nr), ptr(start_point),
                              C.c_uint32(K), ptr(dq), ptr(di), ptr(rgb_out), ptr(g), ptr(dg),
@@ -714,7 +731,8 @@ def trace_vorotracing_bwd(points, diffuse, specular, density, adjacency, offsets
                              C.c_uint32(max_intersections), ptr(points_grad), ptr(diffuse_grad),
                              ptr(specular_grad), ptr(density_grad), ptr(perr), ptr(ws),
                              C.c_uint64(wsb), _path_arg(path, nr),
-                             C.c_uint32(1 if overwrite else 0), ptr(err), stream_ptr(dev)),
+                             C.c_uint32((1 if overwrite else 0) | (2 if keep_workspace else 0)),
+                             ptr(err), stream_ptr(dev)),
           "vt_trace_bwd")
     if _CHECK_ERRORS:
         _check_err(err)

@@ -9,7 +9,11 @@ Training: every rank renders its own rays against the same scene, and the
 per-cell gradients are summed across ranks with one NCCL all-reduce of a
 flat fp32 bucket [points 3N | density N | diffuse 3R^2 N | specular 3R^2 N]
 (``GradBucket``).  The backward kernel writes straight into views of the
-bucket, so the reduction needs no packing copy.
+bucket, so the reduction needs no packing copy.  ``GradBucket.allreduce_``
+is that reduction with NCCL; ``PeerGradReducer`` fuses it with the
+backward's compaction pass in one kernel over peer memory (CUDA IPC,
+NVLink): each rank reads its slice of every rank's backward workspace, sums
+in rank order and writes the result into every rank's bucket.
 """
 from __future__ import annotations
 
@@ -61,3 +65,93 @@ class GradBucket:
     @property
     def nbytes(self) -> int:
         return self.flat.numel() * self.flat.element_size()
+
+
+class PeerGradReducer:
+    """All-reduce of a GradBucket fused with the backward's compaction, over
+    the peer memory of the ranks of one node (vt_grad_allreduce_peer).
+
+    Every rank allocates its backward workspace here and maps the other
+    ranks' workspaces and buckets (CUDA IPC handles exchanged through the
+    process group).  A step is
+
+        trace_vorotracing_bwd(..., grads=bucket.views(), accumulate=False,
+                              workspace=red.workspace, keep_workspace=True)
+        red.reduce_()
+
+    ``reduce_`` brackets the kernel with two one-element all-reduces of the
+    process group, stream-ordered fences: the first orders every rank's
+    backward before any peer reads its workspace, the second every rank's
+    peer stores before the buckets are read and the workspaces reused.  The
+    kernel itself never waits on another GPU.  fp32 attributes only."""
+
+    def __init__(self, bucket: GradBucket, res: int, group=None):
+        import ctypes as C
+
+        import torch.distributed as dist
+
+        from . import _lib
+
+        self.bucket = bucket
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        if self.world > _lib.PEER_MAX:
+            raise RuntimeError(f"PeerGradReducer: at most {_lib.PEER_MAX} ranks")
+        if bucket.flat.dtype != torch.float32:
+            raise RuntimeError("PeerGradReducer: fp32 buckets only")
+        L = _lib.lib()
+        dev = bucket.flat.device
+        wsb = int(L.vt_trace_bwd_workspace_bytes(C.c_uint32(bucket.n), C.c_int(res)))
+        self.workspace = torch.empty(wsb, dtype=torch.uint8, device=dev)
+        mine = []
+        for t in (self.workspace, bucket.flat):
+            h = (C.c_uint8 * 64)()
+            off = C.c_uint64(0)
+            _lib.check(L.vt_ipc_handle(C.c_void_p(t.data_ptr()), h, C.byref(off)), "vt_ipc_handle")
+            mine.append((bytes(h), int(off.value)))
+        table = [None] * self.world
+        dist.all_gather_object(table, mine, group=group)
+        self._opened = []
+        g = _lib.VtPeerGrads()
+        g.world, g.num_points, g.res = self.world, bucket.n, res
+        for k in range(self.world):
+            if k == self.rank:
+                ws_p, b_p = self.workspace.data_ptr(), bucket.flat.data_ptr()
+            else:
+                ptrs = []
+                for handle, off in table[k]:
+                    base = C.c_void_p()
+                    _lib.check(L.vt_ipc_open((C.c_uint8 * 64).from_buffer_copy(handle),
+                                             C.byref(base)), "vt_ipc_open")
+                    self._opened.append(base.value)
+                    ptrs.append(base.value + off)
+                ws_p, b_p = ptrs
+            g.workspace[k] = ws_p
+            g.bucket[k] = b_p
+        self._args = g
+        self._fence = torch.zeros(1, dtype=torch.int32, device=dev)
+
+    def reduce_(self):
+        import ctypes as C
+
+        import torch.distributed as dist
+
+        from . import _lib
+
+        dist.all_reduce(self._fence, group=self.group)
+        _lib.check(_lib.lib().vt_grad_allreduce_peer(C.byref(self._args), C.c_uint32(self.rank),
+                                                     _lib.stream_ptr(self.bucket.flat.device)),
+                   "vt_grad_allreduce_peer")
+        dist.all_reduce(self._fence, group=self.group)
+        return self.bucket
+
+    def close(self):
+        import ctypes as C
+
+        from . import _lib
+
+        torch.cuda.synchronize()
+        for base in self._opened:
+            _lib.lib().vt_ipc_close(C.c_void_p(base))
+        self._opened = []
