@@ -230,6 +230,7 @@ def training_leg(ws, rank, dev, steps, allreduce="peer"):
            "allreduce_ms_per_step": r["allreduce_ms"],
            "allreduce_bus_gbs": r["allreduce_bus_gbs"], "grad_bucket_bytes": r["bucket_bytes"],
            "allreduce": r["allreduce"], "peer_check": r["peer_check"],
+           "peer_fallback": r["peer_fallback"],
            "scaling": "weak", "clocks": r["clocks"],
            "config": {"workload": bc.C4_WORKLOAD, "sites": w["n"],
                       "rays_per_step_per_gpu": w["nr"],

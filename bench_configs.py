@@ -214,8 +214,28 @@ def c4_setup(ws, rank, dev, n_sites=None, attrs_on_device=False, allreduce="peer
     if ws > 1 and allreduce == "peer":
         from vorotracing_b200.shard import PeerGradReducer
 
-        w["reducer"] = PeerGradReducer(bucket, c["res"])
-        w["peer_check"] = _check_peer_reduce(w)
+        # every rank takes the same branch: the setup's outcome is agreed on
+        # through the process group before anything depends on it
+        red, why = None, None
+        try:
+            red = PeerGradReducer(bucket, c["res"])
+        except RuntimeError as e:
+            why = f"peer mapping failed: {e}"
+        ok = torch.tensor([0 if red is None else 1], dtype=torch.int32, device=dev)
+        torch.distributed.all_reduce(ok, op=torch.distributed.ReduceOp.MIN)
+        if int(ok.item()) == 1:
+            w["reducer"] = red
+            chk = _check_peer_reduce(w)
+            w["peer_check"] = chk
+            if not chk["rel"] <= 1e-4:  # agreed: every rank computed the same buckets
+                why = f"peer result differs from NCCL's (rel {chk['rel']:.3g})"
+        elif why is None:
+            why = "peer mapping failed on another rank"
+        if why is not None:
+            if red is not None:
+                red.close()
+            w["reducer"], w["allreduce"] = None, "nccl"
+            w["peer_fallback"] = why
     return w
 
 
@@ -311,7 +331,7 @@ def c4_measure(args, ws, dev, w, steps, warmup):
     busbw = (2.0 * (ws - 1) / ws * nbytes / (ar_ms * 1e-3) / 1e9) if ws > 1 and ar_ms > 0 else None
     return dict(ms_total=ms, ms_per_step=ms / steps, clocks=clocks, allreduce_ms=ar_ms,
                 allreduce_bus_gbs=busbw, bucket_bytes=nbytes, allreduce=w["allreduce"],
-                peer_check=w.get("peer_check"),
+                peer_check=w.get("peer_check"), peer_fallback=w.get("peer_fallback"),
                 rays_per_s=w["nr"] * ws * steps / (ms * 1e-3))
 
 
@@ -326,7 +346,7 @@ def run_c4(args, ws, rank, dev):
     r = c4_measure(args, ws, dev, w, args.steps, args.warmup)
     extra = {"allreduce_ms_per_step": r["allreduce_ms"],
              "allreduce_bus_gbs": r["allreduce_bus_gbs"], "allreduce": r["allreduce"],
-             "peer_check": r["peer_check"]}
+             "peer_check": r["peer_check"], "peer_fallback": r["peer_fallback"]}
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         import oracle
 
