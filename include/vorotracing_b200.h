@@ -229,28 +229,37 @@ VT_API vt_status vt_ipc_close(void *base);
 
 #define VT_PEER_MAX 8
 /* Every rank's backward workspace (written by vt_trace_bwd with
- * VT_BWD_KEEP_WORKSPACE) and flat f32 gradient bucket [points 3N | density N |
- * diffuse 3R^2 N | specular 3R^2 N], as device addresses valid on the
- * calling GPU (its own, or peers' opened with vt_ipc_open).  fp32 attributes
- * only. */
+ * VT_BWD_KEEP_WORKSPACE), flat f32 gradient bucket [points 3N | density N |
+ * diffuse 3R^2 N | specular 3R^2 N] and staging buffer (world slots of
+ * vt_peer_staging_floats(num_points, res, world) floats), as device
+ * addresses valid on the calling GPU (its own, or peers' opened with
+ * vt_ipc_open).  Only the buckets and staging buffers are accessed across
+ * GPUs.  fp32 attributes only. */
 typedef struct {
     uint32_t world;
     uint32_t num_points;
     int32_t res;
     const void *workspace[VT_PEER_MAX];
     float *bucket[VT_PEER_MAX];
+    float *staging[VT_PEER_MAX];
 } vt_peer_grads;
-/* The all-reduce of the training step, fused with the workspace compaction:
- * rank `rank` sums its 1/world share of every gradient (texels and sites
- * from the workspaces, densities from the buckets) over the ranks in rank
- * order 0..world-1 and writes the sums into that share of every rank's bucket
- * by peer stores, so every rank ends with bit-identical buckets.  Every
- * rank's backward must be complete before the call (e.g. a stream-ordered
- * collective as a fence), and no rank may read its bucket or reuse its
- * workspace until every rank's call has completed.  Replaces the
- * vt_trace_bwd compaction plus an NCCL all-reduce of the bucket. */
+/* Floats in one staging slot: the largest rank's share of the bucket. */
+VT_API uint64_t vt_peer_staging_floats(uint32_t num_points, int res, uint32_t world);
+/* The all-reduce of the training step, fused with the workspace compaction,
+ * in two phases over peer memory.  Rank r owns a contiguous 1/world share of
+ * the bucket.  Phase 0: rank r compacts its own workspace (and copies its
+ * densities) and writes every other rank's share of it into slot r of that
+ * rank's staging buffer (peer stores).  Phase 1: rank r sums its share over
+ * the ranks in rank order 0..world-1 (its own workspace, the other ranks'
+ * staging slots) and writes the sums into that share of every rank's bucket
+ * (peer stores), so every rank ends with bit-identical buckets.  Ordering is
+ * the caller's: every rank's phase 0 must be complete before any rank's
+ * phase 1 (e.g. a stream-ordered collective as a fence), and every rank's
+ * phase 1 before a bucket is read or a staging buffer written again.  The
+ * kernels never wait on another GPU.  Replaces the vt_trace_bwd compaction
+ * plus an NCCL all-reduce of the bucket. */
 VT_API vt_status vt_grad_allreduce_peer(const vt_peer_grads *grads, uint32_t rank,
-                                        vt_stream stream);
+                                        uint32_t phase, vt_stream stream);
 
 /* ---- cameras (ray generation for the benchmark views) ---- */
 

@@ -25,7 +25,7 @@ def _dev(a):
     return torch.from_numpy(np.ascontiguousarray(a)).cuda()
 
 
-@pytest.mark.parametrize("world", [2, 3])
+@pytest.mark.parametrize("world", [1, 2, 3])
 def test_peer_allreduce_matches_rank_order_sum(c1_scene, c1_rays, world):
     from vorotracing_b200 import _lib
     from vorotracing_b200.cuda import _ops
@@ -68,14 +68,18 @@ def test_peer_allreduce_matches_rank_order_sum(c1_scene, c1_rays, world):
     want = expect[0].clone()
     for r in range(1, world):
         want += expect[r]
+    slot = int(L.vt_peer_staging_floats(C.c_uint32(n), C.c_int(res), C.c_uint32(world)))
+    stagings = [torch.full((world * slot,), float("nan"), device="cuda") for _ in range(world)]
     g = _lib.VtPeerGrads()
     g.world, g.num_points, g.res = world, n, res
     for k in range(world):
         g.workspace[k] = wss[k].data_ptr()
         g.bucket[k] = buckets[k].flat.data_ptr()
-    for r in range(world):
-        _lib.check(L.vt_grad_allreduce_peer(C.byref(g), C.c_uint32(r), _lib.stream_ptr()),
-                   "vt_grad_allreduce_peer")
+        g.staging[k] = stagings[k].data_ptr()
+    for phase in (0, 1):  # every rank's phase 0 before any phase 1
+        for r in range(world):
+            _lib.check(L.vt_grad_allreduce_peer(C.byref(g), C.c_uint32(r), C.c_uint32(phase),
+                                                _lib.stream_ptr()), "vt_grad_allreduce_peer")
     torch.cuda.synchronize()
     assert want.abs().sum() > 0
     for b in buckets:
@@ -88,10 +92,12 @@ def test_peer_allreduce_rejects_bad_arguments():
     L = _lib.lib()
     g = _lib.VtPeerGrads()
     g.world, g.num_points, g.res = 9, 10, 8
-    assert L.vt_grad_allreduce_peer(C.byref(g), C.c_uint32(0), None) != 0
+    assert L.vt_grad_allreduce_peer(C.byref(g), C.c_uint32(0), C.c_uint32(0), None) != 0
     assert b"world" in L.vt_last_error()
     g.world = 2
-    assert L.vt_grad_allreduce_peer(C.byref(g), C.c_uint32(2), None) != 0
+    assert L.vt_grad_allreduce_peer(C.byref(g), C.c_uint32(2), C.c_uint32(0), None) != 0
     assert b"rank" in L.vt_last_error()
-    assert L.vt_grad_allreduce_peer(C.byref(g), C.c_uint32(0), None) != 0
+    assert L.vt_grad_allreduce_peer(C.byref(g), C.c_uint32(0), C.c_uint32(2), None) != 0
+    assert b"phase" in L.vt_last_error()
+    assert L.vt_grad_allreduce_peer(C.byref(g), C.c_uint32(0), C.c_uint32(0), None) != 0
     assert b"buffers missing" in L.vt_last_error()

@@ -35,7 +35,8 @@ PEER_MAX = 8
 
 class VtPeerGrads(C.Structure):
     _fields_ = [("world", C.c_uint32), ("num_points", C.c_uint32), ("res", C.c_int32),
-                ("workspace", C.c_void_p * PEER_MAX), ("bucket", C.c_void_p * PEER_MAX)]
+                ("workspace", C.c_void_p * PEER_MAX), ("bucket", C.c_void_p * PEER_MAX),
+                ("staging", C.c_void_p * PEER_MAX)]
 
 
 def load(path: str = LIB_PATH, require_all: bool = True):
@@ -56,7 +57,7 @@ def load(path: str = LIB_PATH, require_all: bool = True):
         for name in exported_symbols():
             getattr(L, name)  # every declared entry point must be exported
     for name in ("vt_bvh_nodes_bytes", "vt_bvh_workspace_bytes", "vt_morton_workspace_bytes",
-                 "vt_trace_bwd_workspace_bytes"):
+                 "vt_trace_bwd_workspace_bytes", "vt_peer_staging_floats"):
         if hasattr(L, name):
             getattr(L, name).restype = C.c_uint64
     return L

@@ -3,16 +3,21 @@
 // After the backward (vt_trace_bwd with VT_BWD_KEEP_WORKSPACE) every rank
 // holds its texel and site gradient sums in its padded fp32 workspace (one
 // float4 per texel / site) and its density gradients in its flat bucket.
-// The reference trains on one GPU; here the replacement for "compact the
-// workspace into the bucket, then all-reduce the bucket with NCCL" is one
-// kernel per rank: rank r owns a 1/world slice of every array, reads that
-// slice from all ranks' workspaces and buckets (peer loads over NVLink), sums
-// in rank order, drops the padding and writes the result into the slice of
-// every rank's bucket (peer stores).  The workspace bytes cross NVLink once
-// and the local compaction pass disappears.  Slices are disjoint, so no two
-// ranks write the same words; ordering with the backward and with the next
-// step is the caller's (stream-ordered fences), and the kernel itself never
-// waits on another GPU.
+// The reference trains on one GPU; here "compact the workspace into the
+// bucket, then all-reduce the bucket with NCCL" becomes two kernels per rank
+// over peer memory, every cross-GPU access a posted store:
+//   phase 0  rank r compacts its workspace (drops the float4 padding) and
+//            writes each other rank's share of the result into slot r of
+//            that rank's staging buffer (a reduce-scatter by stores);
+//   phase 1  rank r sums its own share over the ranks in rank order (its
+//            workspace and the staging slots) and writes the sums into that
+//            share of every rank's bucket (an all-gather by stores).
+// NVLink carries (world-1)/world of the compact bucket twice, the bytes of
+// an ideal all-reduce, and the local compaction pass is folded into phase
+// 0.  Shares are disjoint, so no two ranks write the same words.  Ordering
+// (every phase 0 before any phase 1, every phase 1 before the next use) is
+// the caller's, with stream-ordered fences; the kernels never wait on
+// another GPU.
 #include <cstring>
 
 #include "vt_abi.cuh"
@@ -22,63 +27,119 @@ namespace {
 
 inline size_t a256(size_t x) { return (x + 255) & ~(size_t)255; }
 
-struct PeerArgs {
-    uint32_t world;
-    const float4 *sdiff[VT_PEER_MAX];
-    const float4 *sspec[VT_PEER_MAX];
-    const float4 *spts[VT_PEER_MAX];
-    float *bucket[VT_PEER_MAX];
+// Items in bucket order: sites [0, n), densities [n, 2n), diffuse texels
+// [2n, 2n + ntex), specular texels [2n + ntex, 2n + 2 ntex).  Item i's
+// floats in the bucket start at bucket_off(i) (3 per site or texel, 1 per
+// density), so a contiguous item range is a contiguous bucket range.
+struct Layout {
     uint64_t n, ntex;
-    uint64_t begin, end;  // this rank's slice of the combined item space
+    __host__ __device__ uint64_t bucket_off(uint64_t i) const
+    {
+        if (i < n) return 3 * i;
+        if (i < 2 * n) return 3 * n + (i - n);
+        return 4 * n + 3 * (i - 2 * n);
+    }
+    __host__ __device__ uint64_t items() const { return 2 * n + 2 * ntex; }
 };
 
-// Item space: [0, ntex) diffuse texels, [ntex, 2 ntex) specular texels,
-// [2 ntex, 2 ntex + n) sites, [2 ntex + n, 2 ntex + 2 n) densities.
-template <int W>
-__global__ void __launch_bounds__(256) peer_reduce_kernel(PeerArgs a)
+struct PeerArgs {
+    uint32_t world, rank;
+    Layout L;
+    uint64_t share;                 // items per rank (the last rank may own fewer)
+    uint64_t slot;                  // floats per staging slot
+    const float4 *sdiff, *sspec, *spts;  // this rank's workspace
+    float *bucket[VT_PEER_MAX];
+    float *staging[VT_PEER_MAX];
+};
+
+// This rank's compacted value of item i: up to 3 floats (1 for a density).
+__device__ __forceinline__ int local_item(const PeerArgs &a, uint64_t i, float v[3])
 {
+    const uint64_t n = a.L.n, ntex = a.L.ntex;
+    if (i >= n && i < 2 * n) {
+        v[0] = __ldcs(a.bucket[a.rank] + 3 * n + (i - n));
+        return 1;
+    }
+    const float4 q = i < n ? __ldcs(a.spts + i)
+                           : (i < 2 * n + ntex ? __ldcs(a.sdiff + (i - 2 * n))
+                                               : __ldcs(a.sspec + (i - 2 * n - ntex)));
+    v[0] = q.x;
+    v[1] = q.y;
+    v[2] = q.z;
+    return 3;
+}
+
+// Phase 0: every item outside this rank's share goes, compacted, into slot
+// `rank` of its owner's staging buffer.
+__global__ void __launch_bounds__(256) peer_push_kernel(PeerArgs a)
+{
+    const uint64_t total = a.L.items();
+    const uint64_t mine_b = a.share * a.rank, mine_e = min(total, mine_b + a.share);
     const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
-    const uint64_t n = a.n, ntex = a.ntex;
-    const uint32_t world = W > 0 ? (uint32_t)W : a.world;
-    for (uint64_t it = a.begin + (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; it < a.end;
-         it += stride) {
-        if (it < 2 * ntex + n) {
-            const float4 *const *src;
-            uint64_t i, out;
-            if (it < ntex) {
-                src = a.sdiff;
-                i = it;
-                out = 4 * n + 3 * i;
-            } else if (it < 2 * ntex) {
-                src = a.sspec;
-                i = it - ntex;
-                out = 4 * n + 3 * ntex + 3 * i;
-            } else {
-                src = a.spts;
-                i = it - 2 * ntex;
-                out = 3 * i;
-            }
-            float4 acc = __ldcs(src[0] + i);
-            for (uint32_t k = 1; k < world; ++k) {
-                const float4 v = __ldcs(src[k] + i);
-                acc.x += v.x;
-                acc.y += v.y;
-                acc.z += v.z;
-            }
-            for (uint32_t k = 0; k < world; ++k) {
-                float *o = a.bucket[k] + out;
-                o[0] = acc.x;
-                o[1] = acc.y;
-                o[2] = acc.z;
-            }
-        } else {
-            const uint64_t i = 3 * n + (it - 2 * ntex - n);
-            float acc = __ldcs(a.bucket[0] + i);
-            for (uint32_t k = 1; k < world; ++k) acc += __ldcs(a.bucket[k] + i);
-            for (uint32_t k = 0; k < world; ++k) a.bucket[k][i] = acc;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+        if (i >= mine_b && i < mine_e) continue;
+        const uint32_t owner = (uint32_t)(i / a.share);
+        float v[3] = {0.f, 0.f, 0.f};
+        const int c = local_item(a, i, v);
+        float *dst = a.staging[owner] + (uint64_t)a.rank * a.slot +
+                     (a.L.bucket_off(i) - a.L.bucket_off(a.share * owner));
+        dst[0] = v[0];
+        if (c == 3) {
+            dst[1] = v[1];
+            dst[2] = v[2];
         }
     }
-    // make the peer stores visible before the caller's fence
+    __threadfence_system();
+}
+
+// Phase 1: this rank's share, summed in rank order, into every bucket.
+__global__ void __launch_bounds__(256) peer_reduce_kernel(PeerArgs a)
+{
+    const uint64_t total = a.L.items();
+    const uint64_t b = a.share * a.rank, e = min(total, b + a.share);
+    const uint64_t base = a.L.bucket_off(b);
+    const float *stage = a.staging[a.rank];
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    for (uint64_t i = b + (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < e; i += stride) {
+        const uint64_t off = a.L.bucket_off(i), rel = off - base;
+        float mine[3] = {0.f, 0.f, 0.f};
+        const int c = local_item(a, i, mine);
+        float acc[3] = {0.f, 0.f, 0.f};
+        for (uint32_t k = 0; k < a.world; ++k) {
+            float v[3] = {0.f, 0.f, 0.f};
+            if (k == a.rank) {
+                v[0] = mine[0];
+                v[1] = mine[1];
+                v[2] = mine[2];
+            } else {
+                const float *src = stage + (uint64_t)k * a.slot + rel;
+                v[0] = __ldcs(src);
+                if (c == 3) {
+                    v[1] = __ldcs(src + 1);
+                    v[2] = __ldcs(src + 2);
+                }
+            }
+            if (k == 0) {
+                acc[0] = v[0];
+                acc[1] = v[1];
+                acc[2] = v[2];
+            } else {
+                acc[0] += v[0];
+                if (c == 3) {
+                    acc[1] += v[1];
+                    acc[2] += v[2];
+                }
+            }
+        }
+        for (uint32_t k = 0; k < a.world; ++k) {
+            float *o = a.bucket[k] + off;
+            o[0] = acc[0];
+            if (c == 3) {
+                o[1] = acc[1];
+                o[2] = acc[2];
+            }
+        }
+    }
     __threadfence_system();
 }
 
@@ -132,45 +193,60 @@ extern "C" vt_status vt_ipc_close(void *base)
     return VT_OK;
 }
 
-extern "C" vt_status vt_grad_allreduce_peer(const vt_peer_grads *g, uint32_t rank,
+extern "C" uint64_t vt_peer_staging_floats(uint32_t num_points, int res, uint32_t world)
+{
+    if (world == 0 || num_points == 0 || (res != 4 && res != 8)) return 0;
+    const vt::Layout L{num_points, (uint64_t)num_points * res * res};
+    const uint64_t total = L.items(), share = (total + world - 1) / world;
+    uint64_t m = 0;
+    for (uint32_t r = 0; r < world; ++r) {
+        const uint64_t b = share * r < total ? share * r : total;
+        const uint64_t e = b + share < total ? b + share : total;
+        const uint64_t f = (e == total ? 4 * L.n + 6 * L.ntex : L.bucket_off(e)) - L.bucket_off(b);
+        m = f > m ? f : m;
+    }
+    return (m + 63) & ~(uint64_t)63;  // 256-byte aligned slots
+}
+
+extern "C" vt_status vt_grad_allreduce_peer(const vt_peer_grads *g, uint32_t rank, uint32_t phase,
                                             vt_stream stream)
 {
     VT_REQUIRE(g, "vt_grad_allreduce_peer: null argument");
     VT_REQUIRE(g->world >= 1 && g->world <= VT_PEER_MAX, "vt_grad_allreduce_peer: world %u out of range",
                g->world);
     VT_REQUIRE(rank < g->world, "vt_grad_allreduce_peer: rank %u >= world %u", rank, g->world);
+    VT_REQUIRE(phase <= 1, "vt_grad_allreduce_peer: phase must be 0 or 1");
     VT_REQUIRE(g->res == 4 || g->res == 8, "vt_grad_allreduce_peer: res must be 4 or 8");
     VT_REQUIRE(g->num_points > 0, "vt_grad_allreduce_peer: no points");
+    for (uint32_t k = 0; k < g->world; ++k)
+        VT_REQUIRE(g->bucket[k] && g->staging[k], "vt_grad_allreduce_peer: rank %u buffers missing", k);
+    VT_REQUIRE(g->workspace[rank] && (((uintptr_t)g->workspace[rank]) & 255u) == 0,
+               "vt_grad_allreduce_peer: the workspace must be 256-byte aligned");
     vt::PeerArgs a{};
     a.world = g->world;
-    a.n = g->num_points;
-    a.ntex = (uint64_t)g->num_points * g->res * g->res;
+    a.rank = rank;
+    a.L = vt::Layout{g->num_points, (uint64_t)g->num_points * g->res * g->res};
+    a.share = (a.L.items() + g->world - 1) / g->world;
+    a.slot = vt_peer_staging_floats(g->num_points, g->res, g->world);
+    const char *w = (const char *)g->workspace[rank];
+    a.sdiff = (const float4 *)w;
+    a.sspec = (const float4 *)(w + vt::a256(a.L.ntex * 16));
+    a.spts = (const float4 *)(w + 2 * vt::a256(a.L.ntex * 16));
     for (uint32_t k = 0; k < g->world; ++k) {
-        VT_REQUIRE(g->workspace[k] && g->bucket[k], "vt_grad_allreduce_peer: rank %u buffers missing", k);
-        VT_REQUIRE((((uintptr_t)g->workspace[k]) & 255u) == 0 && (((uintptr_t)g->bucket[k]) & 3u) == 0,
-                   "vt_grad_allreduce_peer: workspace must be 256-byte aligned");
-        const char *w = (const char *)g->workspace[k];
-        a.sdiff[k] = (const float4 *)w;
-        a.sspec[k] = (const float4 *)(w + vt::a256(a.ntex * 16));
-        a.spts[k] = (const float4 *)(w + 2 * vt::a256(a.ntex * 16));
         a.bucket[k] = g->bucket[k];
+        a.staging[k] = g->staging[k];
     }
-    const uint64_t total = 2 * a.ntex + 2 * a.n;
-    const uint64_t share = (total + g->world - 1) / g->world;
-    a.begin = share * rank;
-    a.end = a.begin + share < total ? a.begin + share : total;
-    if (a.begin >= a.end) return VT_OK;
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const uint64_t want = (a.end - a.begin + 255) / 256;
-    const unsigned grid = (unsigned)(want < (uint64_t)sms * 8 ? want : (uint64_t)sms * 8);
+    const uint64_t items = phase == 0 ? a.L.items() : a.share;
+    const uint64_t want = (items + 255) / 256;
+    const unsigned grid = (unsigned)(want < (uint64_t)sms * 8 ? (want ? want : 1) : (uint64_t)sms * 8);
     cudaStream_t s = (cudaStream_t)stream;
-    switch (g->world) {
-    case 2: vt::peer_reduce_kernel<2><<<grid, 256, 0, s>>>(a); break;
-    case 4: vt::peer_reduce_kernel<4><<<grid, 256, 0, s>>>(a); break;
-    case 8: vt::peer_reduce_kernel<8><<<grid, 256, 0, s>>>(a); break;
-    default: vt::peer_reduce_kernel<0><<<grid, 256, 0, s>>>(a); break;
+    if (phase == 0) {
+        if (g->world > 1) vt::peer_push_kernel<<<grid, 256, 0, s>>>(a);
+    } else {
+        vt::peer_reduce_kernel<<<grid, 256, 0, s>>>(a);
     }
-    return vt::check_launch("peer_reduce_kernel");
+    return vt::check_launch("vt_grad_allreduce_peer");
 }

@@ -71,19 +71,21 @@ class PeerGradReducer:
     """All-reduce of a GradBucket fused with the backward's compaction, over
     the peer memory of the ranks of one node (vt_grad_allreduce_peer).
 
-    Every rank allocates its backward workspace here and maps the other
-    ranks' workspaces and buckets (CUDA IPC handles exchanged through the
-    process group).  A step is
+    Every rank allocates its backward workspace and a staging buffer here
+    and maps the other ranks' buckets and staging buffers (CUDA IPC handles
+    exchanged through the process group).  A step is
 
         trace_vorotracing_bwd(..., grads=bucket.views(), accumulate=False,
                               workspace=red.workspace, keep_workspace=True)
         red.reduce_()
 
-    ``reduce_`` brackets the kernel with two one-element all-reduces of the
-    process group, stream-ordered fences: the first orders every rank's
-    backward before any peer reads its workspace, the second every rank's
-    peer stores before the buckets are read and the workspaces reused.  The
-    kernel itself never waits on another GPU.  fp32 attributes only."""
+    ``reduce_`` runs phase 0 (this rank's compacted shares stored into their
+    owners' staging buffers), a fence, phase 1 (this rank's share summed in
+    rank order and stored into every bucket) and a fence.  The fences are
+    one-element all-reduces of the process group, stream-ordered: every
+    rank's phase 0 before any phase 1, every phase 1 before the buckets are
+    read and the staging buffers written again.  The kernels never wait on
+    another GPU.  fp32 attributes only."""
 
     def __init__(self, bucket: GradBucket, res: int, group=None):
         import ctypes as C
@@ -103,9 +105,12 @@ class PeerGradReducer:
         L = _lib.lib()
         dev = bucket.flat.device
         wsb = int(L.vt_trace_bwd_workspace_bytes(C.c_uint32(bucket.n), C.c_int(res)))
+        slot = int(L.vt_peer_staging_floats(C.c_uint32(bucket.n), C.c_int(res),
+                                            C.c_uint32(self.world)))
         self.workspace = torch.empty(wsb, dtype=torch.uint8, device=dev)
+        self.staging = torch.empty(self.world * slot, dtype=torch.float32, device=dev)
         mine = []
-        for t in (self.workspace, bucket.flat):
+        for t in (bucket.flat, self.staging):
             h = (C.c_uint8 * 64)()
             off = C.c_uint64(0)
             _lib.check(L.vt_ipc_handle(C.c_void_p(t.data_ptr()), h, C.byref(off)), "vt_ipc_handle")
@@ -115,9 +120,10 @@ class PeerGradReducer:
         self._opened = []
         g = _lib.VtPeerGrads()
         g.world, g.num_points, g.res = self.world, bucket.n, res
+        g.workspace[self.rank] = self.workspace.data_ptr()
         for k in range(self.world):
             if k == self.rank:
-                ws_p, b_p = self.workspace.data_ptr(), bucket.flat.data_ptr()
+                b_p, s_p = bucket.flat.data_ptr(), self.staging.data_ptr()
             else:
                 ptrs = []
                 for handle, off in table[k]:
@@ -126,9 +132,9 @@ class PeerGradReducer:
                                              C.byref(base)), "vt_ipc_open")
                     self._opened.append(base.value)
                     ptrs.append(base.value + off)
-                ws_p, b_p = ptrs
-            g.workspace[k] = ws_p
+                b_p, s_p = ptrs
             g.bucket[k] = b_p
+            g.staging[k] = s_p
         self._args = g
         self._fence = torch.zeros(1, dtype=torch.int32, device=dev)
 
@@ -139,10 +145,13 @@ class PeerGradReducer:
 
         from . import _lib
 
+        L = _lib.lib()
+        stream = _lib.stream_ptr(self.bucket.flat.device)
+        _lib.check(L.vt_grad_allreduce_peer(C.byref(self._args), C.c_uint32(self.rank),
+                                            C.c_uint32(0), stream), "vt_grad_allreduce_peer")
         dist.all_reduce(self._fence, group=self.group)
-        _lib.check(_lib.lib().vt_grad_allreduce_peer(C.byref(self._args), C.c_uint32(self.rank),
-                                                     _lib.stream_ptr(self.bucket.flat.device)),
-                   "vt_grad_allreduce_peer")
+        _lib.check(L.vt_grad_allreduce_peer(C.byref(self._args), C.c_uint32(self.rank),
+                                            C.c_uint32(1), stream), "vt_grad_allreduce_peer")
         dist.all_reduce(self._fence, group=self.group)
         return self.bucket
 
