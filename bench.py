@@ -275,8 +275,8 @@ def main():
     ap.add_argument("--profile", action="store_true",
                     help="a few untimed steps only (for ncu captures)")
     ap.add_argument("--sites", type=int, default=None,
-                    help="override the configuration's site count (small ncu captures of "
-                         "--config C4; never for a reported number)")
+                    help="override the configuration's site count (small ncu captures with "
+                         "--profile; never for a reported number)")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
@@ -297,7 +297,10 @@ def main():
     from vorotracing_b200 import scene as sc
     from vorotracing_b200.render import InferScene
 
-    s = load_scene(rank, ws)
+    if args.sites is not None and not args.profile:
+        raise SystemExit("--sites is for --profile captures only")
+    s = (load_scene(rank, ws) if args.sites is None
+         else load_scene(rank, ws, adjacency="gpu", n=args.sites))
     d = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
     scene = InferScene(d(s["points"]), d(s["density"]), d(s["adj"]), d(s["offs"]),
                        d(s["diffuse"]), d(s["specular"]), quantize="fp16", sort_morton=True)
