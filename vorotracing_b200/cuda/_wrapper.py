@@ -29,12 +29,13 @@ class TraceVoroTracing(torch.autograd.Function):
     in between), where the reference rebuilds its adj_diff on every call.
 
     The forward also records each ray's first ``path_cap`` steps (cell and
-    segment colour, ``path_cap`` * 16 bytes per ray, held until backward) so
+    segment colour, ``path_cap`` * 16 bytes per ray, held until backward; 384 covers all
+    but a handful of the rays of 3M-site scenes) so
     that the backward enters them without scanning faces or re-reading
     texels; set ``path_cap = 0`` to re-walk instead.  Gradients are the same
     either way."""
 
-    path_cap = 256
+    path_cap = 384
 
     @staticmethod
     def forward(ctx, _points, _diffuse, _specular, _density, _point_adjacency,
