@@ -127,6 +127,18 @@ VT_API vt_status vt_trace_infer_q8(const vt_scene *scene, const uint8_t *diffuse
                             float weight_threshold, uint32_t max_intersections,
                             float cell_skip_threshold, void *rgba, const vt_debug *debug,
                             uint32_t *err, vt_stream stream);
+/* vt_trace_infer_q8 on texels widened to 4 bytes (r, g, b, 0; vt_pad_u8x4):
+ * diffuse/specular (N, 4*res*res) u8, 4-byte aligned.  Same pixels, one
+ * 32-bit load per texel instead of three byte loads.  No reference
+ * counterpart (an internal layout of the reference's q8 maps). */
+VT_API vt_status vt_trace_infer_q8x4(const vt_scene *scene, const void *diffuse,
+                                     const void *specular, int res, float diff_scale,
+                                     float diff_offset, float spec_scale, float spec_offset,
+                                     const float *rays, uint32_t num_rays, const uint32_t *start,
+                                     const uint32_t *ray_perm, float weight_threshold,
+                                     uint32_t max_intersections, float cell_skip_threshold,
+                                     void *rgba, const vt_debug *debug, uint32_t *err,
+                                     vt_stream stream);
 
 /* Depth render (the viewer's depth modes, vorotracing/viewer.py:414-433; no
  * kernel counterpart in the reference, which runs the full training forward
@@ -382,6 +394,9 @@ VT_API vt_status vt_tile_perm(uint32_t height, uint32_t width, uint32_t tile_h, 
                               uint32_t *perm, vt_stream stream);
 /* f32 rgb texels -> binary16 Half4Texel rows (rgb + zero pad). */
 VT_API vt_status vt_pad_f16x4(const float *src, uint64_t texels, void *dst, vt_stream stream);
+/* q8 maps (N, 3*R*R) u8 -> (N, 4*R*R) u8, a zero 4th byte per texel (the
+ * layout of vt_trace_infer_q8x4); texels = N*R*R, dst 4-byte aligned. */
+VT_API vt_status vt_pad_u8x4(const uint8_t *src, uint64_t texels, void *dst, vt_stream stream);
 /* dst = clamp(rint((src - offset) / scale), 0, 255). */
 VT_API vt_status vt_quantize_u8(const float *src, uint64_t count, float scale, float offset,
                                 uint8_t *dst, vt_stream stream);

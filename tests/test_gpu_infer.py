@@ -164,3 +164,26 @@ def test_single_cell_scene():
                                                          device="cuda").view(torch.uint32),
                                        faces, None, 0.01, 1024, 0.0)
     assert out.float().abs().sum().item() == 0.0
+
+
+def test_infer_q8_widened_texels_identical(c1_scene, c1_rays):
+    """The q8 trace on texels widened to 4 bytes (pad_u8x4, the layout
+    InferScene renders from) gives the same pixels, bit for bit, as on the
+    reference's 3-byte layout."""
+    from vorotracing_b200.cuda import _ops
+
+    s = c1_scene
+    dq, ds, do = quantize_u8(s["diffuse"])
+    sq, ss, so = quantize_u8(s["specular"])
+    wide = _ops.pad_u8x4(_dev(dq))
+    w = wide.cpu().numpy().reshape(dq.shape[0], -1, 4)
+    np.testing.assert_array_equal(w[..., :3].reshape(dq.shape), dq)
+    assert not w[..., 3].any()
+    start = _u32(_start(s, c1_rays))
+    pts, adj, offs, den, faces = _gpu_scene(s)
+    args = (den, adj, offs, _dev(c1_rays), start, faces, ds, do, ss, so, 0.01, 1024, 1e-3)
+    a = _ops.trace_vorotracing_infer_q8(pts, _dev(dq), _dev(sq), *args)
+    b = _ops.trace_vorotracing_infer_q8(pts, wide, _ops.pad_u8x4(_dev(sq)), *args)
+    torch.cuda.synchronize()
+    assert torch.equal(a.view(torch.int16), b.view(torch.int16))
+    assert float(a[..., 3].float().mean()) > 0.1

@@ -166,6 +166,38 @@ extern "C" vt_status vt_trace_infer_q8(const vt_scene *scene, const uint8_t *dif
     return vt::set_error(VT_ERR_INVALID, "vt_trace_infer_q8: res must be 4 or 8, got %d", res);
 }
 
+extern "C" vt_status vt_trace_infer_q8x4(const vt_scene *scene, const void *diffuse,
+                                         const void *specular, int res, float diff_scale,
+                                         float diff_offset, float spec_scale, float spec_offset,
+                                         const float *rays, uint32_t num_rays,
+                                         const uint32_t *start, const uint32_t *ray_perm,
+                                         float weight_threshold, uint32_t max_intersections,
+                                         float cell_skip_threshold, void *rgba,
+                                         const vt_debug *debug, uint32_t *err, vt_stream stream)
+{
+    vt::InferArgs a;
+    vt_status st = vt::fill_args(a, scene, rays, num_rays, start, ray_perm, weight_threshold,
+                                 max_intersections, cell_skip_threshold, rgba, debug, err,
+                                 "vt_trace_infer_q8x4");
+    if (st != VT_OK) return st;
+    VT_REQUIRE(diffuse && specular, "vt_trace_infer_q8x4: null textures");
+    VT_REQUIRE((((uintptr_t)diffuse | (uintptr_t)specular) & 3u) == 0,
+               "vt_trace_infer_q8x4: textures must be 4-byte aligned");
+    if (num_rays == 0) return VT_OK;
+    cudaStream_t s = (cudaStream_t)stream;
+    if (res == 8) {
+        vt::TexQ8x4<8> t{(const uint32_t *)diffuse, (const uint32_t *)specular, diff_scale,
+                         diff_offset, spec_scale, spec_offset};
+        return vt::launch_infer<8>(a, t, debug != nullptr, s);
+    }
+    if (res == 4) {
+        vt::TexQ8x4<4> t{(const uint32_t *)diffuse, (const uint32_t *)specular, diff_scale,
+                         diff_offset, spec_scale, spec_offset};
+        return vt::launch_infer<4>(a, t, debug != nullptr, s);
+    }
+    return vt::set_error(VT_ERR_INVALID, "vt_trace_infer_q8x4: res must be 4 or 8, got %d", res);
+}
+
 // ---------------------------------------------------------------- depth
 namespace vt {
 

@@ -70,6 +70,35 @@ template <int R> struct TexQ8 {
     }
 };
 
+// q8 texels widened to one 4-byte word each (bytes r, g, b, 0; vt_pad_u8x4):
+// one 32-bit load per texel instead of three byte loads, same values.
+template <int R> struct TexQ8x4 {
+    const uint32_t *diffuse;  // (N, R*R) words
+    const uint32_t *specular;
+    float dscale, doffset, sscale, soffset;
+    __device__ __forceinline__ V3 logits(uint32_t cell, const Bilin &d, const Bilin &s) const
+    {
+        const uint32_t *dp = diffuse + (size_t)cell * (R * R);
+        const uint32_t *sp = specular + (size_t)cell * (R * R);
+        const uint32_t a[4] = {__ldg(dp + d.i00), __ldg(dp + d.i10), __ldg(dp + d.i01),
+                               __ldg(dp + d.i11)};
+        const uint32_t b[4] = {__ldg(sp + s.i00), __ldg(sp + s.i10), __ldg(sp + s.i01),
+                               __ldg(sp + s.i11)};
+        float r[3];
+#pragma unroll
+        for (int c = 0; c < 3; ++c) {
+            float dv[4], sv[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                dv[k] = fmaf(dscale, (float)((a[k] >> (8 * c)) & 0xffu), doffset);
+                sv[k] = fmaf(sscale, (float)((b[k] >> (8 * c)) & 0xffu), soffset);
+            }
+            r[c] = blend(d, dv[0], dv[1], dv[2], dv[3]) + blend(s, sv[0], sv[1], sv[2], sv[3]);
+        }
+        return mk(r[0], r[1], r[2]);
+    }
+};
+
 template <int R, class Tex> struct InferInteg {
     Ray ray;
     Tex tex;

@@ -191,6 +191,16 @@ __global__ void pad_f16x4_kernel(const float *__restrict__ src, uint64_t texels,
     dst[i] = o;
 }
 
+// (N*R^2 texels x 3 bytes) -> one 4-byte word per texel, 4th byte zero
+__global__ void pad_u8x4_kernel(const uint8_t *__restrict__ src, uint64_t texels,
+                                uint32_t *__restrict__ dst)
+{
+    uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= texels) return;
+    const uint8_t *s = src + i * 3;
+    dst[i] = (uint32_t)__ldg(s) | ((uint32_t)__ldg(s + 1) << 8) | ((uint32_t)__ldg(s + 2) << 16);
+}
+
 __global__ void quantize_kernel(const float *__restrict__ src, uint64_t count, float scale,
                                 float offset, uint8_t *__restrict__ dst)
 {
@@ -320,6 +330,15 @@ extern "C" vt_status vt_pad_f16x4(const float *src, uint64_t texels, void *dst, 
     pad_f16x4_kernel<<<vt::grid_for(texels, 256), 256, 0, (cudaStream_t)stream>>>(src, texels,
                                                                                    (uint2 *)dst);
     return vt::check_launch("vt_pad_f16x4");
+}
+
+extern "C" vt_status vt_pad_u8x4(const uint8_t *src, uint64_t texels, void *dst, vt_stream stream)
+{
+    VT_REQUIRE(src && dst && ((uintptr_t)dst & 3u) == 0, "vt_pad_u8x4: bad arguments");
+    if (texels == 0) return VT_OK;
+    pad_u8x4_kernel<<<vt::grid_for(texels, 256), 256, 0, (cudaStream_t)stream>>>(src, texels,
+                                                                                  (uint32_t *)dst);
+    return vt::check_launch("vt_pad_u8x4");
 }
 
 extern "C" vt_status vt_quantize_u8(const float *src, uint64_t count, float scale, float offset,

@@ -212,14 +212,18 @@ def trace_vorotracing_infer_q8(points, diffuse, specular, density, adjacency, of
     if specular.dtype != torch.uint8:
         _fail("q8 inference kernel requires uint8 specular")
     q8 = (float(diff_scale), float(diff_offset), float(spec_scale), float(spec_offset))
+    # (N, 4R^2) maps are this package's widened texels (pad_u8x4), read with
+    # one 32-bit load per texel; (N, 3R^2) is the reference's layout
+    wide = diffuse.dim() == 2 and diffuse.size(1) in (4 * 16, 4 * 64)
     return _infer_common(points, diffuse, specular, density, adjacency, offsets, rays,
                          start_point, adjacent_diff, ray_perm, weight_threshold,
-                         max_intersections, cell_skip_threshold, q8, debug, out, host_io)
+                         max_intersections, cell_skip_threshold, q8, debug, out, host_io,
+                         q8_wide=wide)
 
 
 def _infer_common(points, diffuse, specular, density, adjacency, offsets, rays, start_point,
                   adjacent_diff, ray_perm, wt, max_int, skip, q8, debug, out=None,
-                  host_io=False):
+                  host_io=False, q8_wide=False):
     if rays.size(-1) != 6:
         _fail("rays must have 6 as the last dimension")
     if host_io:
@@ -236,8 +240,9 @@ def _infer_common(points, diffuse, specular, density, adjacency, offsets, rays, 
     if diffuse.size(0) != n or specular.size(0) != n or density.numel() != n:
         _fail("diffuse, specular, density must each have num_points rows")
     faces = _resolve_faces(adjacent_diff, adjacency, points, offsets)
-    res = _res_from(diffuse, 3 if q8 else 4)
-    if _res_from(specular, 3 if q8 else 4) != res:
+    channels = 3 if (q8 and not q8_wide) else 4
+    res = _res_from(diffuse, channels)
+    if _res_from(specular, channels) != res:
         _fail("diffuse and specular octahedral resolutions must match")
     perm = None
     if ray_perm is not None and ray_perm.numel():
@@ -271,7 +276,8 @@ def _infer_common(points, diffuse, specular, density, adjacency, offsets, rays, 
                                   C.c_float(wt), C.c_uint32(max_int), C.c_float(skip),
                                   rgba_p, dbg, ptr(err), stream)
     else:
-        st = L.vt_trace_infer_q8(C.byref(scene), ptr(diffuse), ptr(specular), C.c_int(res),
+        fn = L.vt_trace_infer_q8x4 if q8_wide else L.vt_trace_infer_q8
+        st = fn(C.byref(scene), ptr(diffuse), ptr(specular), C.c_int(res),
                                  *[C.c_float(v) for v in q8], rays_p, C.c_uint32(nr),
                                  ptr(start_point), ptr(perm), C.c_float(wt), C.c_uint32(max_int),
                                  C.c_float(skip), rgba_p, dbg, ptr(err), stream)
@@ -450,6 +456,19 @@ def pad_f16x4(tex: torch.Tensor) -> torch.Tensor:
     out = torch.empty((n, tex.size(1) // 3 * 4), dtype=torch.float16, device=tex.device)
     check(lib().vt_pad_f16x4(ptr(tex), C.c_uint64(tex.numel() // 3), ptr(out),
                              stream_ptr(tex.device)), "vt_pad_f16x4")
+    return out
+
+
+def pad_u8x4(tex: torch.Tensor) -> torch.Tensor:
+    """(N, 3R^2) uint8 q8 map -> (N, 4R^2) uint8 with a zero 4th byte per
+    texel, the widened layout the q8 trace reads with 32-bit loads."""
+    tex = tex.contiguous()
+    if tex.dtype != torch.uint8 or tex.dim() != 2 or tex.size(1) % 3:
+        _fail("pad_u8x4 expects an (N, 3R^2) uint8 map")
+    n, texels = tex.size(0), tex.numel() // 3
+    out = torch.empty((n, tex.size(1) // 3 * 4), dtype=torch.uint8, device=tex.device)
+    check(lib().vt_pad_u8x4(ptr(tex), C.c_uint64(texels), ptr(out), stream_ptr(tex.device)),
+          "vt_pad_u8x4")
     return out
 
 

@@ -36,6 +36,10 @@ class InferScene:
             raise ValueError(f"Invalid quantization method: {quantize}")
         if sort_morton:
             self._reorder_by_morton()
+        if quantize == "q8":
+            # widened copies (a zero 4th byte per texel) for 32-bit texel loads
+            self.diffuse_q8x4 = _ops.pad_u8x4(self.diffuse_q8)
+            self.specular_q8x4 = _ops.pad_u8x4(self.specular_q8)
         self.bvh = _ops.NNBVH()
         self.bvh.build(self.primal_points)
         self.adjacent_diff = _ops.prefetch_faces(self.primal_points, self.point_adjacency,
@@ -89,7 +93,7 @@ class InferScene:
             start_point = torch.broadcast_to(start_point, rays.shape[:-1])
         if self.quantize == "q8":
             return _ops.trace_vorotracing_infer_q8(
-                self.primal_points, self.diffuse_q8, self.specular_q8, self.density,
+                self.primal_points, self.diffuse_q8x4, self.specular_q8x4, self.density,
                 self.point_adjacency, self.point_adjacency_offsets, rays, start_point,
                 self.adjacent_diff, self.diff_scale, self.diff_offset, self.spec_scale,
                 self.spec_offset, weight_threshold, max_intersections, cell_skip_threshold,
