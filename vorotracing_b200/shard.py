@@ -121,20 +121,26 @@ class PeerGradReducer:
         g = _lib.VtPeerGrads()
         g.world, g.num_points, g.res = self.world, bucket.n, res
         g.workspace[self.rank] = self.workspace.data_ptr()
-        for k in range(self.world):
-            if k == self.rank:
-                b_p, s_p = bucket.flat.data_ptr(), self.staging.data_ptr()
-            else:
-                ptrs = []
-                for handle, off in table[k]:
-                    base = C.c_void_p()
-                    _lib.check(L.vt_ipc_open((C.c_uint8 * 64).from_buffer_copy(handle),
-                                             C.byref(base)), "vt_ipc_open")
-                    self._opened.append(base.value)
-                    ptrs.append(base.value + off)
-                b_p, s_p = ptrs
-            g.bucket[k] = b_p
-            g.staging[k] = s_p
+        try:
+            for k in range(self.world):
+                if k == self.rank:
+                    b_p, s_p = bucket.flat.data_ptr(), self.staging.data_ptr()
+                else:
+                    ptrs = []
+                    for handle, off in table[k]:
+                        base = C.c_void_p()
+                        _lib.check(L.vt_ipc_open((C.c_uint8 * 64).from_buffer_copy(handle),
+                                                 C.byref(base)), "vt_ipc_open")
+                        self._opened.append(base.value)
+                        ptrs.append(base.value + off)
+                    b_p, s_p = ptrs
+                g.bucket[k] = b_p
+                g.staging[k] = s_p
+        except RuntimeError:
+            for base in self._opened:  # unmap what was mapped before the failure
+                L.vt_ipc_close(C.c_void_p(base))
+            self._opened = []
+            raise
         self._args = g
         self._fence = torch.zeros(1, dtype=torch.int32, device=dev)
 
