@@ -111,6 +111,7 @@ template <class AT, int R, int F, int M>
 __global__ void __launch_bounds__(kTrainBlock, VT_BWD_MIN_BLOCKS)
     bwd_kernel(TrainCommon a, TexPlain<AT, R> tex, BwdIn<AT> b)
 {
+    __shared__ typename BwdInteg<AT, R, F>::AggLane agg[kTrainBlock];
     uint32_t r = blockIdx.x * blockDim.x + threadIdx.x;
     if (r >= a.num_rays) return;
     uint32_t L = 0;
@@ -172,6 +173,7 @@ __global__ void __launch_bounds__(kTrainBlock, VT_BWD_MIN_BLOCKS)
     I.sspec = b.sspec;
     I.spts = b.spts;
     I.sperr = b.sperr;
+    I.agg = agg + (threadIdx.x & ~31u);
     I.prev_geom = I.prev_grad = I.cur_grad = I.next_grad = mk(0.f, 0.f, 0.f);
     I.prev_idx = 0xffffffffu;
     float tu, tv;

@@ -181,60 +181,73 @@ template <class AT, int R, int F = kBwdDepth | kBwdDist | kBwdErr> struct BwdInt
     AT *perr;
     V3 prev_geom, prev_grad, cur_grad, next_grad;
     uint32_t prev_idx;
+    // This warp's 32 staging slots in shared memory (texel aggregation).
+    struct AggLane {
+        float4 wd, ws, dl;
+    };
+    AggLane *agg;
 
     __device__ __forceinline__ uint32_t textured() const { return ntex; }
 
-    __device__ __forceinline__ void scatter4(float4 *g, uint32_t cell, const Bilin &b, V3 dl) const
+    // Both texel scatters of a textured segment with warp aggregation.  A
+    // warp's rays are neighbouring pixels that enter the same cells at the
+    // same step (about 3 lanes per distinct cell on C2) with nearly equal
+    // specular and often equal diffuse footprints, so lanes scattering into
+    // the same cell with the same four texels (matched among the converged
+    // lanes) sum their weighted contributions first and the group's lowest
+    // lane issues the four float4 reductions.  The sums go through shared
+    // memory: every lane of a group stages its weights and its dl in its
+    // slot, and each group's leader adds its members' terms in lane order.
+    // All groups of the warp are summed at once by their leaders (a shuffle
+    // loop would run once per group, the groups one after another).
+    __device__ __forceinline__ static unsigned long long footprint_key(uint32_t cell,
+                                                                       const Bilin &b)
     {
-        float4 *base = g + (size_t)cell * (R * R);
-        atomicAdd(base + b.i00, make_float4(b.w00 * dl.x, b.w00 * dl.y, b.w00 * dl.z, 0.0f));
-        atomicAdd(base + b.i10, make_float4(b.w10 * dl.x, b.w10 * dl.y, b.w10 * dl.z, 0.0f));
-        atomicAdd(base + b.i01, make_float4(b.w01 * dl.x, b.w01 * dl.y, b.w01 * dl.z, 0.0f));
-        atomicAdd(base + b.i11, make_float4(b.w11 * dl.x, b.w11 * dl.y, b.w11 * dl.z, 0.0f));
+        return ((unsigned long long)cell << 32) |
+               (uint32_t)((b.i00 & 0xff) | (b.i10 & 0xff) << 8 | (b.i01 & 0xff) << 16 |
+                          (b.i11 & 0xff) << 24);
     }
 
-    // scatter4 with warp aggregation: the lanes scattering into the same cell
-    // with the same four texels (the converged lanes here, as for a
-    // coalesced group) sum their contributions first, by shuffles within the
-    // group, and the group's first lane issues the four reductions.  A warp's
-    // rays are neighbouring pixels that enter the same cells at the same step
-    // (about 3 lanes per distinct cell on C2) with nearly equal specular and
-    // often equal diffuse footprints, and the L2 reductions are what bounds
-    // the backward (C2 scene: 10.6 -> 9.6 ms).
-    __device__ __forceinline__ void scatter4_grouped(float4 *g, uint32_t cell, const Bilin &b,
-                                                     V3 dl) const
+    template <bool kSpec>
+    __device__ __forceinline__ void leader_scatter4(float4 *g, uint32_t cell, const Bilin &b,
+                                                    V3 dl, unsigned grp) const
+    {
+        float4 s00 = make_float4(b.w00 * dl.x, b.w00 * dl.y, b.w00 * dl.z, 0.0f);
+        float4 s10 = make_float4(b.w10 * dl.x, b.w10 * dl.y, b.w10 * dl.z, 0.0f);
+        float4 s01 = make_float4(b.w01 * dl.x, b.w01 * dl.y, b.w01 * dl.z, 0.0f);
+        float4 s11 = make_float4(b.w11 * dl.x, b.w11 * dl.y, b.w11 * dl.z, 0.0f);
+        for (unsigned m = grp & (grp - 1); m; m &= m - 1) {
+            const AggLane &o = agg[__ffs(m) - 1];
+            const float4 w = kSpec ? o.ws : o.wd;
+            const float4 d = o.dl;
+            s00.x += w.x * d.x; s00.y += w.x * d.y; s00.z += w.x * d.z;
+            s10.x += w.y * d.x; s10.y += w.y * d.y; s10.z += w.y * d.z;
+            s01.x += w.z * d.x; s01.y += w.z * d.y; s01.z += w.z * d.z;
+            s11.x += w.w * d.x; s11.y += w.w * d.y; s11.z += w.w * d.z;
+        }
+        float4 *base = g + (size_t)cell * (R * R);
+        atomicAdd(base + b.i00, s00);
+        atomicAdd(base + b.i10, s10);
+        atomicAdd(base + b.i01, s01);
+        atomicAdd(base + b.i11, s11);
+    }
+
+    __device__ __forceinline__ void scatter_grouped(uint32_t cell, const Bilin &bd, V3 dl) const
     {
         const unsigned act = __activemask();
-        const unsigned long long key =
-            ((unsigned long long)cell << 32) |
-            (uint32_t)((b.i00 & 0xff) | (b.i10 & 0xff) << 8 | (b.i01 & 0xff) << 16 |
-                       (b.i11 & 0xff) << 24);
-        const unsigned grp = __match_any_sync(act, key);
-        if (__popc(grp) == 1) {
-            scatter4(g, cell, b, dl);
-            return;
+        const unsigned me = 1u << (threadIdx.x & 31);
+        const unsigned gd = __match_any_sync(act, footprint_key(cell, bd));
+        const unsigned gs = __match_any_sync(act, footprint_key(cell, spec));
+        if ((gd | gs) != me) {
+            AggLane &o = agg[threadIdx.x & 31];
+            o.wd = make_float4(bd.w00, bd.w10, bd.w01, bd.w11);
+            o.ws = make_float4(spec.w00, spec.w10, spec.w01, spec.w11);
+            o.dl = make_float4(dl.x, dl.y, dl.z, 0.0f);
         }
-        const int me = threadIdx.x & 31;
-        const int leader = __ffs(grp) - 1;
-        float4 s00 = make_float4(0.f, 0.f, 0.f, 0.f), s10 = s00, s01 = s00, s11 = s00;
-        for (unsigned m = grp; m; m &= m - 1) {
-            const int src = __ffs(m) - 1;
-            const float w00 = __shfl_sync(grp, b.w00, src), w10 = __shfl_sync(grp, b.w10, src);
-            const float w01 = __shfl_sync(grp, b.w01, src), w11 = __shfl_sync(grp, b.w11, src);
-            const float x = __shfl_sync(grp, dl.x, src), y = __shfl_sync(grp, dl.y, src);
-            const float z = __shfl_sync(grp, dl.z, src);
-            s00.x += w00 * x; s00.y += w00 * y; s00.z += w00 * z;
-            s10.x += w10 * x; s10.y += w10 * y; s10.z += w10 * z;
-            s01.x += w01 * x; s01.y += w01 * y; s01.z += w01 * z;
-            s11.x += w11 * x; s11.y += w11 * y; s11.z += w11 * z;
-        }
-        if (me == leader) {
-            float4 *base = g + (size_t)cell * (R * R);
-            atomicAdd(base + b.i00, s00);
-            atomicAdd(base + b.i10, s10);
-            atomicAdd(base + b.i01, s01);
-            atomicAdd(base + b.i11, s11);
-        }
+        __syncwarp(act);
+        if ((gd & (me - 1)) == 0) leader_scatter4<false>(sdiff, cell, bd, dl, gd);
+        if ((gs & (me - 1)) == 0) leader_scatter4<true>(sspec, cell, spec, dl, gs);
+        __syncwarp(act);  // the slots are written again at the next segment
     }
 
     __device__ __forceinline__ void add_site(uint32_t idx, V3 v) const
@@ -363,8 +376,7 @@ template <class AT, int R, int F = kBwdDepth | kBwdDist | kBwdErr> struct BwdInt
             V3 dl = mk((dLdrgb.x * rgb.x) * (1.0f - rgb.x), (dLdrgb.y * rgb.y) * (1.0f - rgb.y),
                        (dLdrgb.z * rgb.z) * (1.0f - rgb.z));
             if (sdiff) {
-                scatter4_grouped(sdiff, cell, db, dl);
-                scatter4_grouped(sspec, cell, spec, dl);
+                scatter_grouped(cell, db, dl);
             } else {
                 scatter(ddiff, cell, db, dl);
                 scatter(dspec, cell, spec, dl);
