@@ -12,7 +12,7 @@ namespace vt {
 
 constexpr int kTrainBlock = 128;
 #ifndef VT_BWD_MIN_BLOCKS
-#define VT_BWD_MIN_BLOCKS 5  // measured on C4: 20.35 -> 19.68 ms per backward (40 B of spills; 6 is slower)
+#define VT_BWD_MIN_BLOCKS 4  // C4 replay backward: 4 blocks 15.38 ms, 5 blocks 16.27 ms, 6 blocks 16.55 ms (same box)
 #endif
 #ifndef VT_FWD_MIN_BLOCKS
 #define VT_FWD_MIN_BLOCKS 8  // measured: 6.98 -> 6.41 ms on the C2 scene (fp32, tile order)
